@@ -1,0 +1,73 @@
+"""Seeded synthetic structures of the benchmark configurations (no public dataset is used; the structures are
+procedural).  Water: H2O molecules (O-H 0.9572 A, H-O-H 104.52 deg) with uniformly random orientations, the O atom of
+each molecule on a cubic grid (spacing 3.104 A) jittered by N(0, 0.05 A), periodic cubic box.  Alloy: bcc lattice
+(a = 3.0 A) with N(0, 0.1 A) displacements and a uniformly drawn element per site.
+
+Species are returned as atomic numbers; ``species_columns`` maps them to the model's one-hot columns.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+WATER_SPACING = 3.104
+ALLOY_Z = (3, 8, 11, 12, 13, 14, 16, 20, 22, 26, 27, 28, 29, 30, 40, 42)
+MASS = {1: 1.008, 8: 15.999}
+
+
+def _random_rotations(rng: np.random.Generator, n: int) -> np.ndarray:
+    q = rng.normal(size=(n, 4))
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    w, x, y, z = q.T
+    return np.stack([
+        np.stack([1 - 2 * (y * y + z * z), 2 * (x * y - z * w), 2 * (x * z + y * w)], -1),
+        np.stack([2 * (x * y + z * w), 1 - 2 * (x * x + z * z), 2 * (y * z - x * w)], -1),
+        np.stack([2 * (x * z - y * w), 2 * (y * z + x * w), 1 - 2 * (x * x + y * y)], -1)], 1)
+
+
+def water_box(nx: int, ny: int | None = None, nz: int | None = None, seed: int = 0,
+              spacing: float = WATER_SPACING, jitter: float = 0.05):
+    """(positions fp64 [3 n_mol, 3], atomic numbers int [3 n_mol] (O, H, H per molecule), box fp64 [3])."""
+    ny = nx if ny is None else ny
+    nz = nx if nz is None else nz
+    rng = np.random.default_rng(seed)
+    g = np.stack(np.meshgrid(np.arange(nx), np.arange(ny), np.arange(nz), indexing="ij"), -1).reshape(-1, 3)
+    n = g.shape[0]
+    centre = g * spacing + rng.normal(scale=jitter, size=(n, 3))
+    half = math.radians(104.52) / 2.0
+    d = 0.9572
+    body = np.array([[0.0, 0.0, 0.0], [d * math.sin(half), d * math.cos(half), 0.0],
+                     [-d * math.sin(half), d * math.cos(half), 0.0]])
+    R = _random_rotations(rng, n)
+    pos = centre[:, None, :] + np.einsum("nij,aj->nai", R, body)
+    box = np.array([nx, ny, nz], dtype=np.float64) * spacing
+    Z = np.tile(np.array([8, 1, 1], dtype=np.int64), n)
+    return np.remainder(pos.reshape(-1, 3), box), Z, box
+
+
+def alloy_bcc(n: int = 60, a: float = 3.0, seed: int = 0, disp: float = 0.1, zs=ALLOY_Z):
+    rng = np.random.default_rng(seed)
+    g = np.stack(np.meshgrid(np.arange(n), np.arange(n), np.arange(n), indexing="ij"), -1).reshape(-1, 3)
+    base = np.concatenate([g, g + 0.5], 0) * a
+    pos = base + rng.normal(scale=disp, size=base.shape)
+    box = np.full(3, n * a)
+    Z = np.asarray(zs, dtype=np.int64)[rng.integers(0, len(zs), size=pos.shape[0])]
+    return np.remainder(pos, box), Z, box
+
+
+def species_columns(Z, atomic_numbers) -> np.ndarray:
+    """Model one-hot column of every atom (index into atomic_numbers)."""
+    lut = {int(z): i for i, z in enumerate(atomic_numbers)}
+    return np.array([lut[int(z)] for z in np.asarray(Z)], dtype=np.int64)
+
+
+def maxwell_boltzmann(Z, temperature: float, seed: int = 0) -> np.ndarray:
+    """Velocities (A/fs) at the given temperature with zero total momentum."""
+    kB = 8.617333262e-5                                    # eV / K
+    amu = 1.0364269e-4                                     # eV fs^2 / A^2 per amu
+    m = np.array([MASS.get(int(z), 2.0 * int(z)) for z in Z]) * amu
+    rng = np.random.default_rng(seed)
+    v = rng.normal(size=(len(Z), 3)) * np.sqrt(kB * temperature / m)[:, None]
+    v -= (m[:, None] * v).sum(0) / m.sum()
+    return v
