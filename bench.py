@@ -1,0 +1,311 @@
+#!/usr/bin/env python
+"""Force-evaluation throughput of the B200 three-pass MACE (the BASELINE metric: atoms/s per force evaluation on the
+1.03M-atom water box, plus the roofline fraction of the dominant kernel).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config water_1m]
+
+A step is one full force evaluation (pass A, H1 exchange, pass B, G1 exchange, pass C, output) of the configuration's
+synthetic structure with random-init weights (seed 0; no dataset or checkpoint is used).  `value` times steps on
+inputs already resident in HBM (the pair list is 2.2 GB of fp64 vectors, larger than L2, so no explicit flush);
+`e2e` times the reference-facing call ThreePassMLIAP.compute_forces(data) with pinned host buffers, the host->device
+copies of the pair list and the device->host copies of energies and pair forces inside the timed region.
+`--impl reference` times the CPU fp64 restatement of the reference's algorithm (oracle/, the reference itself cannot
+be installed: mace-torch / e3nn / cuEquivariance are absent) on a bounded sample of the same workload.
+Multi-GPU (torchrun): each rank evaluates its own copy of the configuration (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "mace-million_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "force-eval atoms/sec at 1.03M-atom water, 1/2/4/8 B200; % of HBM/TC roofline"
+CONFIGS = {
+    "water_1m": dict(kind="water", n=70, seed=0, model_seed=0,
+                     desc="1,029,000-atom water box: 343,000 H2O on a 70^3 grid spaced 3.104 A (box 217.28 A)"),
+    "water_24k": dict(kind="water", n=20, seed=0, model_seed=0, desc="24,000-atom water box (20^3 H2O)"),
+    "water_192": dict(kind="water", n=4, seed=0, model_seed=0, desc="192-atom water box (4^3 H2O)"),
+    "alloy_432k": dict(kind="alloy", n=60, seed=0, model_seed=1, desc="432,000-atom 16-element bcc alloy"),
+}
+# Algorithmic FLOPs per edge of each edge kernel, counted from the algorithm (C = 128 channels, 86 / 16 CG terms,
+# 10 / 4 paths, D = 1280 / 512 spline columns at 8 flops each): forward 8 D + 2 C T + C nW, layer-2 backward
+# 6 C T + 8 D, layer-1 backward 4 C 16 + 8 D.
+FLOPS_PER_EDGE = {"edge_l1_fwd": 8 * 512 + 2 * 128 * 16 + 128 * 4,
+                  "edge_l1_bwd": 4 * 128 * 16 + 8 * 512,
+                  "edge_l2_fwd": 8 * 1280 + 2 * 128 * 86 + 128 * 10,
+                  "edge_l2_bwd": 6 * 128 * 86 + 8 * 1280}
+# edge-kernel launches per evaluation: pass A l1_fwd, pass B l2_fwd + l2_bwd, pass C l1_fwd + l1_bwd
+EDGE_PASSES = {"edge_l1_fwd": 2, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="water_1m", choices=list(CONFIGS))
+    ap.add_argument("--chunk", type=int, default=16384)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=6, help="water molecules per box edge of the CPU sample")
+    return ap.parse_args()
+
+
+def build_structure(cfg):
+    from mace_onegpu import structures as S
+
+    if cfg["kind"] == "water":
+        return S.water_box(cfg["n"], seed=cfg["seed"])
+    return S.alloy_bcc(cfg["n"], seed=cfg["seed"])
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(self.idx)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline(cfg, n_side: int):
+    """The oracle (fp64 torch restatement of the three-pass evaluation, 512-knot tables) on a water box of
+    n_side^3 molecules, all host threads.  Returns (atoms/s, seconds, cores, atoms)."""
+    import dataclasses
+
+    import torch
+
+    from mace_onegpu import model as M
+    from mace_onegpu import neighbors as NB
+    from mace_onegpu import structures as S
+    from oracle import mace_ref
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    m = M.default_model(cfg["model_seed"])
+    if cfg["kind"] == "water":
+        pos, Z, box = S.water_box(n_side, seed=cfg["seed"])
+    else:
+        pos, Z, box = S.alloy_bcc(max(n_side, 5), seed=cfg["seed"])
+    cols = S.species_columns(Z, m.arch.atomic_numbers)
+    pi, pj, rij = NB.neighbor_list(pos, box, m.arch.r_max)
+    ref = mace_ref.MaceRef(m.params(), dataclasses.asdict(m.arch), spline_knots=512)
+    t0 = time.perf_counter()
+    ref.three_pass(pi, pj, rij, cols, len(Z), 16384)
+    dt = time.perf_counter() - t0
+    return len(Z) / dt, dt, cores, len(Z)
+
+
+def run_reference(args, cfg, rank):
+    if rank != 0:
+        return
+    vals = []
+    for k in range(args.warmup + args.steps):
+        v, dt, cores, n = cpu_baseline(cfg, args.cpu_sample)
+        if k >= args.warmup:
+            vals.append((v, dt))
+    value = statistics.median(v for v, _ in vals)
+    ms = statistics.median(dt for _, dt in vals) * 1e3
+    sample = (f"oracle fp64 three-pass (512-knot tables) on a {cfg['kind']} box of {n} atoms "
+              f"({args.cpu_sample}^3 molecules), per-atom throughput of the O(N) evaluation")
+    line = {"metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
+            "config": {"workload": args.config, "description": cfg["desc"], "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "atoms/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ B200 arm
+def main():
+    args = parse()
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from mace_onegpu import _native as N
+    from mace_onegpu import model as M
+    from mace_onegpu import neighbors as NB
+    from mace_onegpu import structures as S
+    from mace_onegpu.engine import ThreePassEngine
+    from mace_onegpu.mliap_data import MLIAPData
+    from mace_onegpu.mliap_threepass import ThreePassMLIAP
+
+    m = M.default_model(cfg["model_seed"])
+    pos, Z, box = build_structure(cfg)
+    cols = torch.as_tensor(S.species_columns(Z, m.arch.atomic_numbers))
+    pi, pj, rij = NB.neighbor_list(pos, box, m.arch.r_max, device=dev)
+    n = len(Z)
+    P = int(pi.numel())
+    elems = cols.to(dev)
+    eng = ThreePassEngine(m, sorted(set(cols.tolist())), chunk=args.chunk, device=dev)
+
+    def step():
+        plan = eng.plan(pi, pj, rij, elems, n, n)
+        return eng.evaluate(plan)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    clk = ClockSampler(local)
+    clk.start()
+    N.timing(True)
+    launches0 = N.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = N.launch_count() - launches0
+    kern = N.timing(False)
+    clocks = clk.stop()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_per_step = ms / args.steps
+    value = n * world * args.steps / (ms * 1e-3)
+
+    # roofline of the dominant kernel (FP32 SIMT edge kernels: FLOP/s against the measured FFMA issue ceiling)
+    dom = max((k for k in kern if k in FLOPS_PER_EDGE), key=lambda k: kern[k][0])
+    dom_ms, dom_launches = kern[dom]
+    flops = FLOPS_PER_EDGE[dom] * P * EDGE_PASSES[dom] * args.steps
+    achieved = flops / (dom_ms * 1e-3) / 1e12 if dom_ms > 0 else 0.0
+    scratch = torch.zeros(1, device=dev)
+    pk = N.c_f64()
+    N.check(N.lib().mace_b200_ffma_peak(2000, N.ptr(scratch), N.byref(pk), torch.cuda.current_stream().cuda_stream),
+            "ffma_peak")
+    peak = pk.value
+
+    # e2e through the reference-facing ML-IAP call, host buffers, copies in the timed region
+    e2e = None
+    if not args.no_e2e:
+        mli = ThreePassMLIAP(m, chunk=args.chunk)
+        hpi = pi.cpu().pin_memory()
+        hpj = pj.cpu().pin_memory()
+        hrij = rij.cpu().pin_memory()
+        hel = cols.clone().pin_memory()
+        data = MLIAPData(hpi, hpj, hrij, hel, n, host_outputs=True)
+        for _ in range(max(1, args.warmup)):
+            mli.compute_forces(data)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            mli.compute_forces(data)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            tt = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ems = float(tt.item())
+        e2e = {"value": n * world * args.steps / (ems * 1e-3), "unit": "atoms/s",
+               "h2d_bytes_per_step": int(P * (4 + 4 + 24) + n * 8), "d2h_bytes_per_step": int(n * 8 + P * 24)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt, cores, na = cpu_baseline(cfg, args.cpu_sample)
+        cpu = {"value": v, "unit": "atoms/s", "cores": cores, "kind": "port",
+               "sample": f"oracle fp64 three-pass (512-knot tables) on a {na}-atom {cfg['kind']} box "
+                         f"({args.cpu_sample}^3 molecules), {dt:.1f} s"}
+
+    if rank == 0:
+        kinds = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps} for k, v in kern.items()}
+        line = {"metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": args.config, "description": cfg["desc"], "atoms_per_gpu": n, "pairs_per_gpu": P,
+                           "chunk": args.chunk, "spline_knots": 512, "model": "MACE-MPA-0-medium architecture, random init",
+                           "parallelism": "replicas" if world > 1 else "single", "l2": "inputs larger than L2 (no flush)"},
+                "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "traffic": None,
+                             "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",
+                             "flops_per_edge": FLOPS_PER_EDGE[dom]},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,210 @@
+/* mace_b200.h — C ABI of the sm_100a three-pass MACE force evaluation (libmace_b200.so).
+ *
+ * The drop-in boundary of the reference (ShiQiaoL/mace-million, package mace_onegpu) is Python:
+ * ThreePassMLIAP.compute_forces(data) (mace_onegpu/mliap_threepass.py:444-616) behind LAMMPS
+ * `pair_style mliap unified`, which calls Triton kernels (conv_spline.py, spline_w.py) and cuEquivariance
+ * (fused_conv.py) per receiver chunk.  This library replaces those kernels and the chunk loops.  Every entry point
+ * takes plain device pointers, sizes and a cudaStream_t (passed as void*), never torch types; all device memory is
+ * owned by the caller (the Python host allocates it with torch).  Each entry point returns 0 on success or a
+ * negative MB_E_* code; mace_b200_last_error() gives the message of the last failure on the calling thread.
+ * Kernels never trap: device-side input checks set bits in the caller's status word (MB_ST_*), read by the host
+ * at pass ends.
+ *
+ * Layouts: features with 128 channels per irrep component are component-major, [atom][component][128] fp32
+ * (h1: 4 components 0e|1o; layer-1 messages 16 components; layer-2 messages 40 components).  Pairs are sorted by
+ * receiver; rowptr is the CSR row pointer over local receivers.
+ */
+#ifndef MACE_B200_H
+#define MACE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MB_ABI_VERSION 1
+
+enum {
+  MB_OK = 0,
+  MB_E_ARG = -1,      /* bad argument (null pointer, size out of range, unsupported width) */
+  MB_E_CUDA = -2,     /* a CUDA runtime call failed */
+  MB_E_STATUS = -3,   /* the device status word reported an input error */
+};
+
+/* device status bits (written by kernels into mb_eval_t.status) */
+enum {
+  MB_ST_BAD_SENDER = 1,
+  MB_ST_BAD_SPECIES = 2,
+  MB_ST_BAD_ROWPTR = 4,
+  MB_ST_NONFINITE = 8,
+  MB_ST_BAD_RECEIVER = 16,
+};
+
+/* Folded, device-resident model (fp32 unless noted).  S = number of species present (compact indices),
+ * C = 128, NT1 / NT2 = symmetric-contraction coefficient counts (mace_b200_sc_layout). */
+typedef struct {
+  int32_t C, S, M;             /* channels, species, spline knots */
+  float r_lo, inv_h, r_max, p_cut;
+  float scale;                 /* ScaleShift scale */
+  const float* tab1;           /* [S*S][M-1][4][C] float4 cubic coefficients of W1 * X1(sender species) */
+  const float* tab2;           /* [S*S][M-1][10][C] float4 cubic coefficients of W2 */
+  const float* wd1;            /* [8] layer-1 density weights / sqrt(8) */
+  const float* wd2;            /* [8] layer-2 density weights / sqrt(8) */
+  const float* M0;             /* [S][4][C][C]  linear_1 o skip_tp_1 per species and l */
+  const float* M0T;            /* transposes */
+  const float* Wp1;            /* [2][C][C]     products[0].linear per l */
+  const float* Wp1T;
+  const float* wr0;            /* [C]           readouts[0] */
+  const float* sc1;            /* [S][NT1][C]   symmetric contraction 1 (L = 0 and L = 1 outputs) */
+  const float* Wup2;           /* [2][C][C]     interactions[1].linear_up per l */
+  const float* Wup2T;
+  const float* Wsk1;           /* [S][C][C]     interactions[1].skip_tp (0e -> 0e) per species */
+  const float* Wsk1T;
+  const float* Wlin2;          /* [10][C][C]    interactions[1].linear per mid entry (scaled by its group) */
+  const float* Wlin2T;
+  const float* sc2;            /* [S][NT2][C]   symmetric contraction 2 (L = 0) */
+  const float* Wp2;            /* [C][C]        products[1].linear */
+  const float* Wp2T;
+  const float* W1r;            /* [C][16]       readouts[1].linear_1 / sqrt(C) */
+  const float* w2r;            /* [16]          readouts[1].linear_2 * cst / sqrt(16) */
+  const double* e0;            /* [S]           E0 + shift per species (fp64) */
+} mb_model_t;
+
+/* One force evaluation: the pair list (receiver-sorted), persistent per-atom state and per-chunk scratch. */
+typedef struct {
+  int32_t nl, nt;              /* local atoms, local + ghost atoms */
+  int64_t P;                   /* pairs */
+  const int32_t* pair_i;       /* [P] receivers (local), non-decreasing */
+  const int32_t* pair_j;       /* [P] senders (local or ghost) */
+  const double* rij;           /* [P][3] edge vectors (receiver - sender convention of the model) */
+  const int32_t* rowptr;       /* [nl+1] CSR over receivers */
+  const int32_t* spec;         /* [nt] compact species index */
+  float* H1;                   /* [nt][4][C]  layer-1 features (ghost rows filled by the forward exchange) */
+  float* X2;                   /* [nt][4][C]  linear_up(H1) of every atom */
+  float* G1;                   /* [nt][4][C]  dE2/dh1 (ghost rows reverse-exchanged onto owners) */
+  float* GX2;                  /* [nt][4][C]  dE2/dX2 accumulated over all chunks */
+  float* PF;                   /* [P][3]      pair forces dE/drij, fp32 accumulator */
+  double* eat;                 /* [nl]        per-atom energies */
+  int32_t chunk;               /* receivers per chunk (scratch capacity) */
+  const int32_t* order;        /* [nl] receivers of every chunk sorted by species (chunk-local indices) */
+  const int32_t* spec_off;     /* HOST array [(n_chunks)*(S+1)]: species segment offsets inside each chunk */
+  float* s_msg;                /* [chunk][40][C] */
+  float* s_x;                  /* [chunk][16][C] */
+  float* s_gx;                 /* [chunk][16][C] */
+  float* s_a;                  /* [chunk][4][C]  */
+  float* s_ga;                 /* [chunk][4][C]  */
+  float* s_h;                  /* [chunk][C]     */
+  float* s_gh;                 /* [chunk][C]     */
+  float* s_sc;                 /* [chunk][C]     */
+  float* s_rho;                /* [chunk] */
+  float* s_grho;               /* [chunk] */
+  uint32_t* status;            /* device status word */
+} mb_eval_t;
+
+/* ---------------------------------------------------------------- library info */
+int mace_b200_abi_version(void);
+const char* mace_b200_last_error(void);
+/* sizeof(mb_model_t), sizeof(mb_eval_t) as compiled into the library (for binding checks). */
+int mace_b200_struct_sizes(int32_t* model_bytes, int32_t* eval_bytes);
+/* Number of kernels this library has launched since it was loaded (all threads). */
+unsigned long long mace_b200_launch_count(void);
+/* Per-kind CUDA-event timing of the pass runners' edge and symmetric-contraction launches (the reference's
+ * per-pass wall timers, mliap_threepass.py:525-585, at kernel granularity).  mace_b200_timing(enable, ms, cnt)
+ * synchronises on the recorded events, writes the accumulated milliseconds and launch counts per kind
+ * (MB_K_*, arrays of MB_NKINDS, either may be null), resets them and switches recording on or off. */
+enum { MB_K_EDGE_L1_FWD = 0, MB_K_EDGE_L1_BWD = 1, MB_K_EDGE_L2_FWD = 2, MB_K_EDGE_L2_BWD = 3, MB_K_SYMCON = 4,
+       MB_NKINDS = 5 };
+int mace_b200_timing(int enable, double* ms_out, long long* count_out);
+/* FP32 FFMA issue ceiling of the current device (TFLOP/s), by an 8-chain FFMA kernel on 8 CTAs per SM (the edge
+ * kernels' roofline denominator; scratch is one device float). */
+int mace_b200_ffma_peak(int32_t iters, float* scratch, double* tflops, void* stream);
+/* Number of symmetric-contraction coefficients per (species, channel) for block 0 (layer 1) or 1 (layer 2), and
+ * the layout fingerprint the host must reproduce when it folds the weights. */
+int mace_b200_sc_layout(int block, int32_t* n_coef, uint64_t* fingerprint);
+
+/* ---------------------------------------------------------------- tables
+ * Replaces conv_spline.build_tables (mace_onegpu/conv_spline.py:230-249) and spline_radial._sample
+ * (mace_onegpu/spline_radial.py:237-272): per ordered species pair p = s_send * S + s_recv, the radial MLP
+ * W(r) = silu(silu(silu(f(r) A0) A1) A2) A3 (f = Bessel x cutoff, fp64) sampled on M knots over [r_lo, r_max] with
+ * dW/dr by central differences (eps = 1e-5 (r_max - r_lo)), times col_scale[p][d] (null = 1).  Outputs TV, TG = h dW/dr
+ * ([P][M][D] fp32, the reference's table format; either may be null) and the float4 cubic form
+ * cubic[P][M-1][D] (a + b t + c t^2 + d t^3 on each interval, fp32 from fp64). */
+int mace_b200_build_tables(const double* A0, const double* A1, const double* A2, const double* A3, int32_t n_in,
+                           int32_t hidden, int32_t D, const double* col_scale, int32_t n_pairs, int32_t M,
+                           double r_lo, double r_max, double p_cut, float* TV, float* TG, float* cubic,
+                           void* stream);
+
+/* ---------------------------------------------------------------- edge kernels (one receiver chunk [a, b))
+ * edge_l1_fwd replaces ConvSpline.forward (mace_onegpu/conv_spline.py:294-301) and the density sum
+ *   (fast_layers.py:179-183): s_msg[i][lm][c] = sum_e T1(r_e, p_e)[l][c] Y_e[lm], s_rho[i] = sum_e tanh(d_e^2).
+ * edge_l2_fwd replaces FusedConvTP.forward (mace_onegpu/fused_conv.py:33-37) fed by SplineW (spline_w.py:30-50):
+ *   s_msg[i][o][c] = sum_e sum_terms coef W2(r_e)[w][c] X2[j_e][k][c] Y_e[m], s_rho[i].
+ * edge_l2_bwd replaces the autograd backward of pass B for the edge part (mliap_threepass.py:549-552 with
+ *   spline_w.py:53-75): given s_gx = dE/dmsg (in s_msg) and s_grho, PF[e] = dE/drij, GX2[j_e] += dE/dX2.
+ * edge_l1_bwd: pass C edge backward (mliap_threepass.py:576-581): PF[e] += dL/drij. */
+int mace_b200_edge_l1_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream);
+int mace_b200_edge_l2_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream);
+int mace_b200_edge_l2_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream);
+int mace_b200_edge_l1_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream);
+
+/* ---------------------------------------------------------------- generic fused convolution (FusedConvTP)
+ * Replaces the cuEquivariance fused convolution behind FusedConvTP.forward (mace_onegpu/fused_conv.py:20-37) and its
+ * autograd backward: out[receiver[e]][o][:] += sum_terms coef W[e][w][:] X[sender[e]][k][:] Y[e][m] with explicit
+ * per-edge weights W [E][nW][128], node features X [n][nX][128], edge attributes Y [E][nY]; terms_wkmo [n_terms][4]
+ * = (w, k, m, o) with coef [n_terms].  out must be zeroed by the caller (accumulated atomically; any edge order).
+ * bwd: given g = dL/dout [n][nO][128] accumulates dX (atomic), dY (atomic) and dW (dW[e] owned per edge); any of the
+ * three may be null.  Out-of-range node indices set MB_ST_BAD_SENDER in *status (may be null) and skip the edge. */
+int mace_b200_conv_tp_fwd(const float* X, int32_t nX, const float* Y, int32_t nY, const float* W, int32_t nW,
+                          const int32_t* sender, const int32_t* receiver, int64_t E, int32_t n_nodes,
+                          const int32_t* terms_wkmo, const float* coef, int32_t n_terms, float* out, int32_t nO,
+                          uint32_t* status, void* stream);
+int mace_b200_conv_tp_bwd(const float* X, int32_t nX, const float* Y, int32_t nY, const float* W, int32_t nW,
+                          const int32_t* sender, const int32_t* receiver, int64_t E, int32_t n_nodes,
+                          const int32_t* terms_wkmo, const float* coef, int32_t n_terms, const float* g, int32_t nO,
+                          float* dX, float* dY, float* dW, uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------- node GEMM
+ * Replaces the cuEquivariance irreps Linear and SpeciesSkip.forward (mace_onegpu/fast_layers.py:96-105):
+ *   Y[atom][yoff + m][:] (+)= alpha_atom * sum_j X[atom][xoff_j + m][:] @ B_j       (m = 0 .. mult-1)
+ * for n_atoms atoms (atom = order ? order[t] : t, t = 0 .. n_atoms-1), K = n_seg * 128, N = 128, B_j [128][128]
+ * row-major (B = [n_seg][128][128]); alpha_atom = 1 / (rho[atom] + 1) when rho is not null.
+ * ldx / ldy are the per-atom strides in floats; accumulate != 0 adds into Y. */
+int mace_b200_node_gemm(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg, const float* B,
+                        float* Y, int64_t ldy, int32_t yoff, int32_t mult, const int32_t* order, int32_t n_atoms,
+                        const float* rho, int32_t accumulate, void* stream);
+
+/* ---------------------------------------------------------------- symmetric contraction
+ * Replaces products[k].symmetric_contractions (mace EquivariantProductBasisBlock, correlation 3).
+ * block 0: x [n][16][C] -> A [n][4][C] (L = 0 | L = 1); block 1: x [n][16][C] -> A [n][C].
+ * bwd: gA -> gx [n][16][C]; when grho is not null also grho[i] = -sum(gx * x) / (rho[i] + 1). */
+int mace_b200_symcon_fwd(const mb_model_t* m, int32_t block, const float* x, float* A, const int32_t* spec_local,
+                         int32_t n, void* stream);
+int mace_b200_symcon_bwd(const mb_model_t* m, int32_t block, const float* x, const float* gA, float* gx,
+                         const int32_t* spec_local, const float* rho, float* grho, int32_t n, void* stream);
+
+/* ---------------------------------------------------------------- three passes (chunk loops in C++)
+ * pass_a: mliap_threepass.py:504-519 (H1[a:b] = layer1 for every chunk), then R1 energies.
+ * x2_all: X2 = linear_up(H1) for all nt atoms (after the forward exchange); zeroes G1 and GX2.
+ * pass_b: mliap_threepass.py:537-553 (layer-2 energy, PF, G1), then G1 += linear_up^T(GX2).
+ * pass_c: mliap_threepass.py:564-587 (loss = E1 + G1 . h1, PF).
+ * finalize: eat += E0 + shift (mliap_threepass.py:589), PFd = PF in fp64 scattered to the caller's pair order
+ *   (perm = receiver-sorted position -> caller position, null = identity), and *fmax_bits (device word, zeroed by
+ *   the caller) = bits of max |PF| as an fp32 (a NaN anywhere gives NaN bits), for the force guard
+ *   (mliap_threepass.py:595-601). */
+int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev, void* stream);
+int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* stream);
+int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* stream);
+int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev, void* stream);
+int mace_b200_finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd,
+                       uint32_t* fmax_bits, void* stream);
+
+/* ---------------------------------------------------------------- halo exchange helpers (mliap_threepass.py:40-55)
+ * pack: buf[k][:] = src[idx[k]][:] (D floats per row); unpack_add: dst[idx[k]][:] += buf[k][:]. */
+int mace_b200_pack_rows(const float* src, const int32_t* idx, int64_t n, int32_t D, float* buf, void* stream);
+int mace_b200_unpack_add_rows(const float* buf, const int32_t* idx, int64_t n, int32_t D, float* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MACE_B200_H */

@@ -1,0 +1,457 @@
+// Edge kernels of the three passes: one CTA per receiver, one thread per channel (C = 128).  Each batch of edges
+// first runs a per-edge prologue (one thread per edge: length, SH, spline interval, density, SH Jacobian) into
+// shared memory; then every thread walks the batch for its channel.  Replaces the reference's ConvSpline
+// (mace_onegpu/conv_spline.py:38-94), SplineW (spline_w.py:30-75) and the cuEquivariance fused convolution with its
+// autograd backward (fused_conv.py:33-37, mliap_threepass.py:549-581).
+#include "common.cuh"
+#include "tp_gen.cuh"
+
+namespace mb {
+
+struct EdgeCtx {
+  Radial rd;
+  int S, nt;
+  int64_t P;
+};
+
+__device__ __forceinline__ EdgeCtx make_ctx(const mb_model_t& m, const mb_eval_t& ev) {
+  EdgeCtx x;
+  x.rd.r_max = m.r_max;
+  x.rd.p = m.p_cut;
+  x.rd.r_lo = m.r_lo;
+  x.rd.inv_h = m.inv_h;
+  x.rd.M = m.M;
+  x.S = m.S;
+  x.nt = ev.nt;
+  x.P = ev.P;
+  return x;
+}
+
+// Common per-edge checks and geometry.  Returns false (and records a status bit) for an edge that must be skipped.
+__device__ __forceinline__ bool edge_geom(const mb_eval_t& ev, const EdgeCtx& x, int64_t e, int i, float3& v, float& r,
+                                          int& j, int& pair) {
+  j = ev.pair_j[e];
+  const int pi = ev.pair_i[e];
+  if (pi != i) {
+    set_status(ev.status, ST_BAD_RECEIVER);
+    return false;
+  }
+  if (j < 0 || j >= x.nt) {
+    set_status(ev.status, ST_BAD_SENDER);
+    return false;
+  }
+  const int ss = ev.spec[j], sr = ev.spec[i];
+  if (ss < 0 || ss >= x.S || sr < 0 || sr >= x.S) {
+    set_status(ev.status, ST_BAD_SPECIES);
+    return false;
+  }
+  const double* rp = ev.rij + 3 * e;
+  v = make_float3((float)rp[0], (float)rp[1], (float)rp[2]);
+  r = sqrtf(v.x * v.x + v.y * v.y + v.z * v.z);
+  if (!(r > 0.f) || !isfinite(r)) {
+    set_status(ev.status, ST_NONFINITE);
+    return false;
+  }
+  pair = ss * x.S + sr;
+  return true;
+}
+
+__device__ __forceinline__ bool row_range(const mb_eval_t& ev, int i, int64_t& e0, int64_t& e1) {
+  e0 = ev.rowptr[i];
+  e1 = ev.rowptr[i + 1];
+  if (e0 < 0 || e1 < e0 || e1 > ev.P) {
+    set_status(ev.status, ST_BAD_ROWPTR);
+    return false;
+  }
+  return true;
+}
+
+// SH values and the Jacobian dY/dv (v = r u): dY/dv = (grad_u Y - u (u . grad_u Y)) / r.
+__device__ __forceinline__ void sh_jacobian(float3 u, float r, float* Y, float* J) {
+  D3 ux = {u.x, 1.f, 0.f, 0.f}, uy = {u.y, 0.f, 1.f, 0.f}, uz = {u.z, 0.f, 0.f, 1.f};
+  D3 Yd[16];
+  sh16<D3>(ux, uy, uz, Yd);
+  const float ir = 1.f / r;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    Y[q] = Yd[q].v;
+    float ug = u.x * Yd[q].dx + u.y * Yd[q].dy + u.z * Yd[q].dz;
+    J[3 * q + 0] = (Yd[q].dx - u.x * ug) * ir;
+    J[3 * q + 1] = (Yd[q].dy - u.y * ug) * ir;
+    J[3 * q + 2] = (Yd[q].dz - u.z * ug) * ir;
+  }
+}
+
+__device__ __forceinline__ float cubic(float4 q, float t) { return fmaf(fmaf(fmaf(q.w, t, q.z), t, q.y), t, q.x); }
+__device__ __forceinline__ float dcubic(float4 q, float t) { return fmaf(fmaf(3.f * q.w, t, 2.f * q.z), t, q.y); }
+
+__device__ __forceinline__ float block_sum128(float v, float* red4) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red4[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return red4[0] + red4[1] + red4[2] + red4[3];
+}
+
+// ------------------------------------------------------------------------------------------------ layer 1 forward
+// s_msg[i][lm][c] = sum_e T1(r_e; pair_e)[l][c] * Y_e[lm];  s_rho[i] = sum_e tanh(d_e^2)
+template <int EB>
+__global__ void __launch_bounds__(128) k_edge_l1_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
+  __shared__ float sY[EB][16];
+  __shared__ int srow[EB];
+  __shared__ float st[EB];
+  __shared__ float red4[4];
+  const EdgeCtx x = make_ctx(m, ev);
+  const int il = blockIdx.x, i = a + il, c = threadIdx.x;
+  int64_t e0, e1;
+  if (!row_range(ev, i, e0, e1)) return;
+  const float4* tab = reinterpret_cast<const float4*>(m.tab1);
+  float acc[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+  float rho = 0.f;
+  for (int64_t base = e0; base < e1; base += EB) {
+    const int n = (int)min((int64_t)EB, e1 - base);
+    __syncthreads();
+    if (c < n) {
+      float3 v;
+      float r;
+      int j, pair;
+      int row = -1;
+      if (edge_geom(ev, x, base + c, i, v, r, j, pair)) {
+        int k;
+        float t;
+        spline_coords(r, x.rd, k, t);
+        row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
+        st[c] = t;
+        const float ir = 1.f / r;
+        float Y[16];
+        sh16<float>(v.x * ir, v.y * ir, v.z * ir, Y);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) sY[c][q] = Y[q];
+        float ed, ded;
+        edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
+        rho += ed;
+      }
+      srow[c] = row;
+    }
+    __syncthreads();
+    for (int q = 0; q < n; ++q) {
+      const int row = srow[q];
+      if (row < 0) continue;
+      const float t = st[q];
+      const float4* rw = tab + row + c;
+      const float T0 = cubic(__ldg(rw), t);
+      const float T1 = cubic(__ldg(rw + MB_C), t);
+      const float T2 = cubic(__ldg(rw + 2 * MB_C), t);
+      const float T3 = cubic(__ldg(rw + 3 * MB_C), t);
+      const float* Y = sY[q];
+      acc[0] = fmaf(T0, Y[0], acc[0]);
+#pragma unroll
+      for (int mm = 1; mm < 4; ++mm) acc[mm] = fmaf(T1, Y[mm], acc[mm]);
+#pragma unroll
+      for (int mm = 4; mm < 9; ++mm) acc[mm] = fmaf(T2, Y[mm], acc[mm]);
+#pragma unroll
+      for (int mm = 9; mm < 16; ++mm) acc[mm] = fmaf(T3, Y[mm], acc[mm]);
+    }
+  }
+  float* out = ev.s_msg + (size_t)il * 16 * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) out[q * MB_C] = acc[q];
+  rho = block_sum128(rho, red4);
+  if (c == 0) ev.s_rho[il] = rho;
+}
+
+// ------------------------------------------------------------------------------------------------ layer 1 backward
+// Pass C: given g = dL/dmsg1 (s_msg, [i][16][C]) and s_grho, PF[e] += dL/dv_e.
+template <int EB>
+__global__ void __launch_bounds__(128) k_edge_l1_bwd(const mb_model_t m, const mb_eval_t ev, int a) {
+  __shared__ float sY[EB][16];
+  __shared__ float sJ[EB][48];
+  __shared__ float su[EB][3];
+  __shared__ float sgd[EB];
+  __shared__ int srow[EB];
+  __shared__ float st[EB];
+  __shared__ float sred[EB][4][3];
+  const EdgeCtx x = make_ctx(m, ev);
+  const int il = blockIdx.x, i = a + il, c = threadIdx.x, warp = c >> 5, lane = c & 31;
+  int64_t e0, e1;
+  if (!row_range(ev, i, e0, e1)) return;
+  const float4* tab = reinterpret_cast<const float4*>(m.tab1);
+  float g[16];
+  const float* gin = ev.s_msg + (size_t)il * 16 * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) g[q] = gin[q * MB_C];
+  const float grho = ev.s_grho[il];
+  for (int64_t base = e0; base < e1; base += EB) {
+    const int n = (int)min((int64_t)EB, e1 - base);
+    __syncthreads();
+    if (c < n) {
+      float3 v;
+      float r;
+      int j, pair;
+      int row = -1;
+      if (edge_geom(ev, x, base + c, i, v, r, j, pair)) {
+        int k;
+        float t;
+        spline_coords(r, x.rd, k, t);
+        row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
+        st[c] = t;
+        const float ir = 1.f / r;
+        float3 u = make_float3(v.x * ir, v.y * ir, v.z * ir);
+        sh_jacobian(u, r, sY[c], sJ[c]);
+        su[c][0] = u.x;
+        su[c][1] = u.y;
+        su[c][2] = u.z;
+        float ed, ded;
+        edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
+        sgd[c] = grho * ded;
+      }
+      srow[c] = row;
+    }
+    __syncthreads();
+    for (int q = 0; q < n; ++q) {
+      const int row = srow[q];
+      if (row < 0) continue;
+      const float t = st[q];
+      const float4* rw = tab + row + c;
+      const float* Y = sY[q];
+      const float* J = sJ[q];
+      float gr = 0.f, gvx = 0.f, gvy = 0.f, gvz = 0.f;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        const float4 cq = __ldg(rw + l * MB_C);
+        const float T = cubic(cq, t);
+        const float dT = dcubic(cq, t) * x.rd.inv_h;
+        float gT = 0.f;
+#pragma unroll
+        for (int mm = l * l; mm < (l + 1) * (l + 1); ++mm) {
+          gT = fmaf(g[mm], Y[mm], gT);
+          const float gy = g[mm] * T;
+          gvx = fmaf(gy, J[3 * mm + 0], gvx);
+          gvy = fmaf(gy, J[3 * mm + 1], gvy);
+          gvz = fmaf(gy, J[3 * mm + 2], gvz);
+        }
+        gr = fmaf(gT, dT, gr);
+      }
+      gvx = fmaf(gr, su[q][0], gvx);
+      gvy = fmaf(gr, su[q][1], gvy);
+      gvz = fmaf(gr, su[q][2], gvz);
+      gvx = warp_sum(gvx);
+      gvy = warp_sum(gvy);
+      gvz = warp_sum(gvz);
+      if (lane == 0) {
+        sred[q][warp][0] = gvx;
+        sred[q][warp][1] = gvy;
+        sred[q][warp][2] = gvz;
+      }
+    }
+    __syncthreads();
+    if (c < n && srow[c] >= 0) {
+      float* pf = ev.PF + 3 * (base + c);
+#pragma unroll
+      for (int d = 0; d < 3; ++d)
+        pf[d] += sred[c][0][d] + sred[c][1][d] + sred[c][2][d] + sred[c][3][d] + sgd[c] * su[c][d];
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ layer 2 forward
+// s_msg[i][o][c] = sum_e sum_t coef_t W2(r_e)[w_t][c] X2[j_e][k_t][c] Y_e[m_t];  s_rho[i]
+template <int EB>
+__global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
+  __shared__ float scy[EB][TP2_NT];
+  __shared__ int srow[EB];
+  __shared__ int ssend[EB];
+  __shared__ float st[EB];
+  __shared__ float red4[4];
+  const EdgeCtx x = make_ctx(m, ev);
+  const int il = blockIdx.x, i = a + il, c = threadIdx.x;
+  int64_t e0, e1;
+  if (!row_range(ev, i, e0, e1)) return;
+  const float4* tab = reinterpret_cast<const float4*>(m.tab2);
+  float acc[TP2_NO];
+#pragma unroll
+  for (int q = 0; q < TP2_NO; ++q) acc[q] = 0.f;
+  float rho = 0.f;
+  for (int64_t base = e0; base < e1; base += EB) {
+    const int n = (int)min((int64_t)EB, e1 - base);
+    __syncthreads();
+    if (c < n) {
+      float3 v;
+      float r;
+      int j, pair;
+      int row = -1;
+      if (edge_geom(ev, x, base + c, i, v, r, j, pair)) {
+        int k;
+        float t;
+        spline_coords(r, x.rd, k, t);
+        row = (pair * (x.rd.M - 1) + k) * TP2_NW * MB_C;
+        st[c] = t;
+        ssend[c] = j;
+        const float ir = 1.f / r;
+        float Y[16];
+        sh16<float>(v.x * ir, v.y * ir, v.z * ir, Y);
+        tp2_cy(Y, scy[c]);
+        float ed, ded;
+        edge_density(r, m.wd2, x.rd.r_max, x.rd.p, ed, ded);
+        rho += ed;
+      }
+      srow[c] = row;
+    }
+    __syncthreads();
+    for (int q = 0; q < n; ++q) {
+      const int row = srow[q];
+      if (row < 0) continue;
+      const float* xs = ev.X2 + (size_t)ssend[q] * 4 * MB_C + c;
+      float X[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) X[k] = __ldg(xs + k * MB_C);
+      tp2_fwd(tab + row + c, st[q], X, scy[q], acc);
+    }
+  }
+  float* out = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < TP2_NO; ++q) out[q * MB_C] = acc[q];
+  rho = block_sum128(rho, red4);
+  if (c == 0) ev.s_rho[il] = rho;
+}
+
+// ------------------------------------------------------------------------------------------------ layer 2 backward
+// Pass B: given g = dE/dmsg2 (s_msg, [i][40][C]) and s_grho: PF[e] += dE/dv_e, GX2[j_e] += dE/dX2.
+template <int EB>
+__global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const mb_eval_t ev, int a) {
+  __shared__ float scy[EB][TP2_NT];
+  __shared__ float sJ[EB][48];
+  __shared__ float su[EB][3];
+  __shared__ float sgd[EB];
+  __shared__ int srow[EB];
+  __shared__ int ssend[EB];
+  __shared__ float st[EB];
+  __shared__ float sred[EB][4][3];
+  const EdgeCtx x = make_ctx(m, ev);
+  const int il = blockIdx.x, i = a + il, c = threadIdx.x, warp = c >> 5, lane = c & 31;
+  int64_t e0, e1;
+  if (!row_range(ev, i, e0, e1)) return;
+  const float4* tab = reinterpret_cast<const float4*>(m.tab2);
+  float g[TP2_NO];
+  const float* gin = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < TP2_NO; ++q) g[q] = gin[q * MB_C];
+  const float grho = ev.s_grho[il];
+  for (int64_t base = e0; base < e1; base += EB) {
+    const int n = (int)min((int64_t)EB, e1 - base);
+    __syncthreads();
+    if (c < n) {
+      float3 v;
+      float r;
+      int j, pair;
+      int row = -1;
+      if (edge_geom(ev, x, base + c, i, v, r, j, pair)) {
+        int k;
+        float t;
+        spline_coords(r, x.rd, k, t);
+        row = (pair * (x.rd.M - 1) + k) * TP2_NW * MB_C;
+        st[c] = t;
+        ssend[c] = j;
+        const float ir = 1.f / r;
+        float3 u = make_float3(v.x * ir, v.y * ir, v.z * ir);
+        float Y[16];
+        sh_jacobian(u, r, Y, sJ[c]);
+        tp2_cy(Y, scy[c]);
+        su[c][0] = u.x;
+        su[c][1] = u.y;
+        su[c][2] = u.z;
+        float ed, ded;
+        edge_density(r, m.wd2, x.rd.r_max, x.rd.p, ed, ded);
+        sgd[c] = grho * ded;
+      }
+      srow[c] = row;
+    }
+    __syncthreads();
+    for (int q = 0; q < n; ++q) {
+      const int row = srow[q];
+      if (row < 0) continue;
+      const int j = ssend[q];
+      const float* xs = ev.X2 + (size_t)j * 4 * MB_C + c;
+      float X[4], gX[4] = {0.f, 0.f, 0.f, 0.f}, gY[16];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) X[k] = __ldg(xs + k * MB_C);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) gY[k] = 0.f;
+      float gr = 0.f;
+      tp2_bwd(tab + row + c, st[q], x.rd.inv_h, X, scy[q], g, gX, gY, gr);
+      float* gxo = ev.GX2 + (size_t)j * 4 * MB_C + c;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) atomicAdd(gxo + k * MB_C, gX[k]);
+      const float* J = sJ[q];
+      float gvx = gr * su[q][0], gvy = gr * su[q][1], gvz = gr * su[q][2];
+#pragma unroll
+      for (int mm = 0; mm < 16; ++mm) {
+        gvx = fmaf(gY[mm], J[3 * mm + 0], gvx);
+        gvy = fmaf(gY[mm], J[3 * mm + 1], gvy);
+        gvz = fmaf(gY[mm], J[3 * mm + 2], gvz);
+      }
+      gvx = warp_sum(gvx);
+      gvy = warp_sum(gvy);
+      gvz = warp_sum(gvz);
+      if (lane == 0) {
+        sred[q][warp][0] = gvx;
+        sred[q][warp][1] = gvy;
+        sred[q][warp][2] = gvz;
+      }
+    }
+    __syncthreads();
+    if (c < n && srow[c] >= 0) {
+      float* pf = ev.PF + 3 * (base + c);
+#pragma unroll
+      for (int d = 0; d < 3; ++d)
+        pf[d] += sred[c][0][d] + sred[c][1][d] + sred[c][2][d] + sred[c][3][d] + sgd[c] * su[c][d];
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ launchers
+static int edge_args(const mb_model_t* m, const mb_eval_t* ev, int a, int b, const char* who) {
+  if (!m || !ev || a < 0 || b > ev->nl || b < a) {
+    set_error("%s: bad chunk [%d, %d)", who, a, b);
+    return MB_E_ARG;
+  }
+  if (m->C != MB_C) {
+    set_error("%s: only C = 128 is supported (got %d)", who, m->C);
+    return MB_E_ARG;
+  }
+  return 0;
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int mace_b200_edge_l1_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
+  if (int rc = edge_args(m, ev, a, b, "edge_l1_fwd")) return rc;
+  if (b == a) return 0;
+  k_edge_l1_fwd<128><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  return check_launch("edge_l1_fwd");
+}
+
+extern "C" int mace_b200_edge_l1_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
+  if (int rc = edge_args(m, ev, a, b, "edge_l1_bwd")) return rc;
+  if (b == a) return 0;
+  k_edge_l1_bwd<64><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  return check_launch("edge_l1_bwd");
+}
+
+extern "C" int mace_b200_edge_l2_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
+  if (int rc = edge_args(m, ev, a, b, "edge_l2_fwd")) return rc;
+  if (b == a) return 0;
+  k_edge_l2_fwd<64><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  return check_launch("edge_l2_fwd");
+}
+
+extern "C" int mace_b200_edge_l2_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
+  if (int rc = edge_args(m, ev, a, b, "edge_l2_bwd")) return rc;
+  if (b == a) return 0;
+  k_edge_l2_bwd<64><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  return check_launch("edge_l2_bwd");
+}

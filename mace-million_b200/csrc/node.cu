@@ -1,0 +1,464 @@
+// Node-side kernels: channel-mixing GEMM (irreps linears, species-block skip), symmetric contraction, readouts,
+// energies, pair-force finalisation and halo row packing.
+#include <float.h>
+
+#include "common.cuh"
+#include "symcon_gen.cuh"
+
+namespace mb {
+
+// ------------------------------------------------------------------------------------------------ GEMM
+// Y[atom][yoff + m][:] (+)= alpha_atom * sum_s X[atom][xoff_s + m][:] @ B_s  (N = 128, K = nseg * 128).
+// Rows r = t * mult + m, atom = order ? order[t] : t.  Tile 64 rows x 128 columns, K step 32, 256 threads,
+// 4 x 8 outputs per thread.  (SIMT fp32 path.)
+struct GemmArgs {
+  const float* X;
+  int64_t ldx;
+  int xoff[4];
+  int nseg;
+  const float* B;
+  float* Y;
+  int64_t ldy;
+  int yoff;
+  int mult;
+  const int* order;
+  int n_atoms;
+  const float* rho;
+  int accumulate;
+};
+
+constexpr int GBM = 64, GBN = 128, GBK = 32;
+
+__global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
+  __shared__ __align__(16) float As[GBK][GBM + 4];
+  __shared__ __align__(16) float Bs[GBK][GBN];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t nrows = (int64_t)g.n_atoms * g.mult;
+  const int64_t r0 = (int64_t)blockIdx.x * GBM;
+  // the A row this thread loads: r = r0 + tid / 4, k sub-block (tid % 4) * 8
+  const int lr = tid >> 2, lk = (tid & 3) * 8;
+  const int64_t rl = r0 + lr;
+  const float* arow = nullptr;
+  if (rl < nrows) {
+    const int64_t t = rl / g.mult;
+    const int mm = (int)(rl - t * g.mult);
+    const int64_t at = g.order ? g.order[t] : t;
+    arow = g.X + at * g.ldx + (int64_t)mm * MB_C + lk;
+  }
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int K = g.nseg * MB_C;
+  for (int k0 = 0; k0 < K; k0 += GBK) {
+    const int seg = k0 / MB_C, kin = k0 - seg * MB_C;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    if (arow) {
+      const float* p = arow + (int64_t)g.xoff[seg] * MB_C + kin;
+      a0 = *reinterpret_cast<const float4*>(p);
+      a1 = *reinterpret_cast<const float4*>(p + 4);
+    }
+    __syncthreads();
+    As[lk + 0][lr] = a0.x;
+    As[lk + 1][lr] = a0.y;
+    As[lk + 2][lr] = a0.z;
+    As[lk + 3][lr] = a0.w;
+    As[lk + 4][lr] = a1.x;
+    As[lk + 5][lr] = a1.y;
+    As[lk + 6][lr] = a1.z;
+    As[lk + 7][lr] = a1.w;
+    const float* bsrc = g.B + (int64_t)k0 * GBN;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = (tid + q * 256) * 4;
+      *reinterpret_cast<float4*>(&Bs[idx / GBN][idx % GBN]) = __ldg(reinterpret_cast<const float4*>(bsrc + idx));
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < GBK; ++kk) {
+      float a[4], b[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + tx * 4]);
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+      b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + ty + 16 * i;
+    if (r >= nrows) continue;
+    const int64_t t = r / g.mult;
+    const int mm = (int)(r - t * g.mult);
+    const int64_t at = g.order ? g.order[t] : t;
+    const float alpha = g.rho ? 1.f / (g.rho[at] + 1.f) : 1.f;
+    float* y = g.Y + at * g.ldy + (int64_t)(g.yoff + mm) * MB_C;
+    float4 v0 = make_float4(acc[i][0] * alpha, acc[i][1] * alpha, acc[i][2] * alpha, acc[i][3] * alpha);
+    float4 v1 = make_float4(acc[i][4] * alpha, acc[i][5] * alpha, acc[i][6] * alpha, acc[i][7] * alpha);
+    float4* y0 = reinterpret_cast<float4*>(y + tx * 4);
+    float4* y1 = reinterpret_cast<float4*>(y + 64 + tx * 4);
+    if (g.accumulate) {
+      float4 o0 = *y0, o1 = *y1;
+      v0.x += o0.x; v0.y += o0.y; v0.z += o0.z; v0.w += o0.w;
+      v1.x += o1.x; v1.y += o1.y; v1.z += o1.z; v1.w += o1.w;
+    }
+    *y0 = v0;
+    *y1 = v1;
+  }
+}
+
+int gemm_launch(const float* X, int64_t ldx, const int32_t* xoff, int nseg, const float* B, float* Y, int64_t ldy,
+                int yoff, int mult, const int32_t* order, int n_atoms, const float* rho, int accumulate,
+                cudaStream_t st) {
+  if (n_atoms <= 0) return 0;
+  if (!X || !B || !Y || !xoff || nseg < 1 || nseg > 4 || mult < 1 || (ldx % 4) || (ldy % 4)) {
+    set_error("node_gemm: bad arguments (nseg %d, mult %d)", nseg, mult);
+    return MB_E_ARG;
+  }
+  GemmArgs g;
+  g.X = X;
+  g.ldx = ldx;
+  for (int s = 0; s < 4; ++s) g.xoff[s] = s < nseg ? xoff[s] : 0;
+  g.nseg = nseg;
+  g.B = B;
+  g.Y = Y;
+  g.ldy = ldy;
+  g.yoff = yoff;
+  g.mult = mult;
+  g.order = order;
+  g.n_atoms = n_atoms;
+  g.rho = rho;
+  g.accumulate = accumulate;
+  const int64_t rows = (int64_t)n_atoms * mult;
+  k_gemm<<<(unsigned)((rows + GBM - 1) / GBM), 256, 0, st>>>(g);
+  return check_launch("node_gemm");
+}
+
+// ------------------------------------------------------------------------------------------------ symmetric contraction
+// One CTA per atom, one thread per channel.  x [n][16][C]; block 0 -> A [n][4][C], block 1 -> A [n][C].
+template <int BLK>
+__global__ void __launch_bounds__(128) k_symcon_fwd(const float* __restrict__ coef, const float* __restrict__ x,
+                                                    float* __restrict__ A, const int* __restrict__ spec, int S) {
+  constexpr int NT = BLK == 0 ? SC0_NT : SC1_NT;
+  constexpr int NO = BLK == 0 ? SC0_NOUT : SC1_NOUT;
+  const int i = blockIdx.x, c = threadIdx.x;
+  const int s = min(max(spec[i], 0), S - 1);
+  float xv[16], out[NO];
+  const float* xp = x + (size_t)i * 16 * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) xv[q] = xp[q * MB_C];
+  const float* cf = coef + (size_t)s * NT * MB_C + c;
+  if constexpr (BLK == 0)
+    sc0_fwd(xv, cf, out);
+  else
+    sc1_fwd(xv, cf, out);
+  float* ap = A + (size_t)i * NO * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < NO; ++q) ap[q * MB_C] = out[q];
+}
+
+template <int BLK>
+__global__ void __launch_bounds__(128) k_symcon_bwd(const float* __restrict__ coef, const float* __restrict__ x,
+                                                    const float* __restrict__ gA, float* __restrict__ gx,
+                                                    const int* __restrict__ spec, int S, const float* __restrict__ rho,
+                                                    float* __restrict__ grho) {
+  constexpr int NT = BLK == 0 ? SC0_NT : SC1_NT;
+  constexpr int NO = BLK == 0 ? SC0_NOUT : SC1_NOUT;
+  __shared__ float red4[4];
+  const int i = blockIdx.x, c = threadIdx.x;
+  const int s = min(max(spec[i], 0), S - 1);
+  float xv[16], ga[NO], gv[16];
+  const float* xp = x + (size_t)i * 16 * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) xv[q] = xp[q * MB_C];
+  const float* gp = gA + (size_t)i * NO * MB_C + c;
+#pragma unroll
+  for (int q = 0; q < NO; ++q) ga[q] = gp[q * MB_C];
+  const float* cf = coef + (size_t)s * NT * MB_C + c;
+  if constexpr (BLK == 0)
+    sc0_bwd(xv, cf, ga, gv);
+  else
+    sc1_bwd(xv, cf, ga, gv);
+  float* op = gx + (size_t)i * 16 * MB_C + c;
+  float dot = 0.f;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    op[q * MB_C] = gv[q];
+    dot = fmaf(gv[q], xv[q], dot);
+  }
+  if (grho) {
+    dot = warp_sum(dot);
+    if ((c & 31) == 0) red4[c >> 5] = dot;
+    __syncthreads();
+    if (c == 0) grho[i] = -(red4[0] + red4[1] + red4[2] + red4[3]) / (rho[i] + 1.f);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ readout 2
+// Per atom: z = h2 @ W1r, e = sum_j silu(z_j) w2r_j;  eat += scale e;  g_h2 = scale * W1r (w2r * silu'(z)).
+__global__ void __launch_bounds__(128) k_readout2(const float* __restrict__ h2, const float* __restrict__ W1r,
+                                                  const float* __restrict__ w2r, float scale, double* __restrict__ eat,
+                                                  float* __restrict__ gh2) {
+  __shared__ float sz[4][16];
+  __shared__ float sg[16];
+  const int i = blockIdx.x, c = threadIdx.x, warp = c >> 5, lane = c & 31;
+  const float h = h2[(size_t)i * MB_C + c];
+  float w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    w[j] = __ldg(W1r + c * 16 + j);
+    float z = warp_sum(h * w[j]);
+    if (lane == 0) sz[warp][j] = z;
+  }
+  __syncthreads();
+  if (c < 32) {
+    float e = 0.f;
+    if (c < 16) {
+      const float z = sz[0][c] + sz[1][c] + sz[2][c] + sz[3][c];
+      const float sig = 1.f / (1.f + expf(-z));
+      const float w2 = __ldg(w2r + c);
+      e = z * sig * w2;
+      sg[c] = scale * w2 * sig * (1.f + z * (1.f - sig));
+    }
+    e = warp_sum(e);
+    if (c == 0) eat[i] += (double)scale * (double)e;
+  }
+  __syncthreads();
+  float g = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) g = fmaf(sg[j], w[j], g);
+  gh2[(size_t)i * MB_C + c] = g;
+}
+
+// R1 energies: eat[i] += scale * H1[i][0][:] . wr0
+__global__ void k_readout1(const float* __restrict__ H1, const float* __restrict__ wr0, float scale, int n,
+                           double* __restrict__ eat) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= n) return;
+  const float* h = H1 + (size_t)warp * 4 * MB_C;
+  float s = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) s = fmaf(h[lane + 32 * q], __ldg(wr0 + lane + 32 * q), s);
+  s = warp_sum(s);
+  if (lane == 0) eat[warp] += (double)scale * (double)s;
+}
+
+// g_h1 = G1r[a + i] + scale * wr0 on the 0e block (pass C, loss = scale R1 + G1 . h1)
+__global__ void k_gh1(const float* __restrict__ G1, const float* __restrict__ wr0, float scale, int n,
+                      float* __restrict__ out) {
+  const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (size_t)n * 4 * MB_C) return;
+  const int comp = (int)((q / MB_C) % 4), c = (int)(q % MB_C);
+  out[q] = G1[q] + (comp == 0 ? scale * __ldg(wr0 + c) : 0.f);
+}
+
+// eat += e0[spec]; PFd[perm[e]] = PF[e] (fp64); fmax = max |PF| (NaN propagates through the unsigned max)
+__global__ void k_finalize(const float* __restrict__ PF, int64_t P, const int64_t* __restrict__ perm,
+                           double* __restrict__ PFd, const int* __restrict__ spec, const double* __restrict__ e0,
+                           int S, int nl, double* __restrict__ eat, unsigned* __restrict__ fmax_bits) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  unsigned mx = 0;
+  for (int64_t e = t; e < P; e += stride) {
+    const int64_t dst = perm ? perm[e] : e;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const float v = PF[3 * e + d];
+      PFd[3 * dst + d] = (double)v;
+      mx = max(mx, __float_as_uint(fabsf(v)));
+    }
+  }
+  for (int64_t i = t; i < nl; i += stride) {
+    const int s = spec[i];
+    eat[i] += (s >= 0 && s < S) ? e0[s] : 0.0;
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0 && mx) atomicMax(fmax_bits, mx);
+}
+
+__global__ void k_pack(const float* __restrict__ src, const int* __restrict__ idx, int64_t n, int D,
+                       float* __restrict__ buf) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= n * D) return;
+  const int64_t k = q / D;
+  buf[q] = src[(int64_t)idx[k] * D + (q - k * D)];
+}
+
+__global__ void k_unpack_add(const float* __restrict__ buf, const int* __restrict__ idx, int64_t n, int D,
+                             float* __restrict__ dst) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= n * D) return;
+  const int64_t k = q / D;
+  atomicAdd(dst + (int64_t)idx[k] * D + (q - k * D), buf[q]);
+}
+
+int symcon_fwd(const mb_model_t* m, int block, const float* x, float* A, const int32_t* spec, int n,
+               cudaStream_t st) {
+  if (n <= 0) return 0;
+  if (block == 0)
+    k_symcon_fwd<0><<<n, 128, 0, st>>>(m->sc1, x, A, spec, m->S);
+  else
+    k_symcon_fwd<1><<<n, 128, 0, st>>>(m->sc2, x, A, spec, m->S);
+  return check_launch("symcon_fwd");
+}
+
+int symcon_bwd(const mb_model_t* m, int block, const float* x, const float* gA, float* gx, const int32_t* spec,
+               const float* rho, float* grho, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  if (grho && !rho) {
+    set_error("symcon_bwd: grho needs rho");
+    return MB_E_ARG;
+  }
+  if (block == 0)
+    k_symcon_bwd<0><<<n, 128, 0, st>>>(m->sc1, x, gA, gx, spec, m->S, rho, grho);
+  else
+    k_symcon_bwd<1><<<n, 128, 0, st>>>(m->sc2, x, gA, gx, spec, m->S, rho, grho);
+  return check_launch("symcon_bwd");
+}
+
+int readout2(const mb_model_t* m, const float* h2, double* eat, float* gh2, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  k_readout2<<<n, 128, 0, st>>>(h2, m->W1r, m->w2r, m->scale, eat, gh2);
+  return check_launch("readout2");
+}
+
+int readout1(const mb_model_t* m, const float* H1, double* eat, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  k_readout1<<<(n + 7) / 8, 256, 0, st>>>(H1, m->wr0, m->scale, n, eat);
+  return check_launch("readout1");
+}
+
+int gh1(const mb_model_t* m, const float* G1, float* out, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  const size_t tot = (size_t)n * 4 * MB_C;
+  k_gh1<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(G1, m->wr0, m->scale, n, out);
+  return check_launch("gh1");
+}
+
+int finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd, unsigned* fmax_bits,
+             cudaStream_t st) {
+  k_finalize<<<1184, 256, 0, st>>>(ev->PF, ev->P, perm, PFd, ev->spec, m->e0, m->S, ev->nl, ev->eat, fmax_bits);
+  return check_launch("finalize");
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int mace_b200_node_gemm(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg, const float* B,
+                                   float* Y, int64_t ldy, int32_t yoff, int32_t mult, const int32_t* order,
+                                   int32_t n_atoms, const float* rho, int32_t accumulate, void* stream) {
+  return gemm_launch(X, ldx, xoff, n_seg, B, Y, ldy, yoff, mult, order, n_atoms, rho, accumulate,
+                     (cudaStream_t)stream);
+}
+
+extern "C" int mace_b200_symcon_fwd(const mb_model_t* m, int32_t block, const float* x, float* A,
+                                    const int32_t* spec_local, int32_t n, void* stream) {
+  if (!m || (block != 0 && block != 1)) {
+    set_error("symcon_fwd: bad block");
+    return MB_E_ARG;
+  }
+  return symcon_fwd(m, block, x, A, spec_local, n, (cudaStream_t)stream);
+}
+
+extern "C" int mace_b200_symcon_bwd(const mb_model_t* m, int32_t block, const float* x, const float* gA, float* gx,
+                                    const int32_t* spec_local, const float* rho, float* grho, int32_t n,
+                                    void* stream) {
+  if (!m || (block != 0 && block != 1)) {
+    set_error("symcon_bwd: bad block");
+    return MB_E_ARG;
+  }
+  return symcon_bwd(m, block, x, gA, gx, spec_local, rho, grho, n, (cudaStream_t)stream);
+}
+
+extern "C" int mace_b200_sc_layout(int block, int32_t* n_coef, uint64_t* fingerprint) {
+  if (block == 0) {
+    if (n_coef) *n_coef = SC0_NT;
+    if (fingerprint) *fingerprint = SC0_FP;
+    return 0;
+  }
+  if (block == 1) {
+    if (n_coef) *n_coef = SC1_NT;
+    if (fingerprint) *fingerprint = SC1_FP;
+    return 0;
+  }
+  set_error("sc_layout: block must be 0 or 1");
+  return MB_E_ARG;
+}
+
+extern "C" int mace_b200_pack_rows(const float* src, const int32_t* idx, int64_t n, int32_t D, float* buf,
+                                   void* stream) {
+  if (n <= 0) return 0;
+  if (!src || !idx || !buf || D <= 0) {
+    set_error("pack_rows: bad arguments");
+    return MB_E_ARG;
+  }
+  k_pack<<<(unsigned)((n * D + 255) / 256), 256, 0, (cudaStream_t)stream>>>(src, idx, n, D, buf);
+  return check_launch("pack_rows");
+}
+
+extern "C" int mace_b200_unpack_add_rows(const float* buf, const int32_t* idx, int64_t n, int32_t D, float* dst,
+                                         void* stream) {
+  if (n <= 0) return 0;
+  if (!buf || !idx || !dst || D <= 0) {
+    set_error("unpack_add_rows: bad arguments");
+    return MB_E_ARG;
+  }
+  k_unpack_add<<<(unsigned)((n * D + 255) / 256), 256, 0, (cudaStream_t)stream>>>(buf, idx, n, D, dst);
+  return check_launch("unpack_add_rows");
+}
+
+// ------------------------------------------------------------------------------------------------ FP32 peak probe
+// Eight independent FFMA chains per thread: the FP32 issue ceiling the SIMT edge kernels are measured against
+// (the measured-peaks file of this pool records HBM and bf16 tensor peaks only).
+namespace mb {
+__global__ void __launch_bounds__(256) k_ffma_peak(float* out, int iters, float a, float b) {
+  float x[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) x[q] = threadIdx.x * 1e-7f + q * 1e-3f;
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) x[q] = fmaf(x[q], a, b);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) s += x[q];
+  if (s == 1234.5f) out[0] = s;
+}
+}  // namespace mb
+
+extern "C" int mace_b200_ffma_peak(int32_t iters, float* scratch, double* tflops, void* stream) {
+  if (!scratch || !tflops || iters <= 0) {
+    set_error("ffma_peak: bad arguments");
+    return MB_E_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int dev = 0, nsm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = nsm * 8;
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  k_ffma_peak<<<blocks, 256, 0, st>>>(scratch, iters, 0.9999999f, 1e-7f);   // warm-up
+  cudaEventRecord(e0, st);
+  k_ffma_peak<<<blocks, 256, 0, st>>>(scratch, iters, 0.9999999f, 1e-7f);
+  cudaEventRecord(e1, st);
+  int rc = check_launch("ffma_peak");
+  cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *tflops = 2.0 * 8 * 16 * (double)iters * blocks * 256 / (ms * 1e-3) / 1e12;
+  return rc;
+}

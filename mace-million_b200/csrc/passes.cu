@@ -1,0 +1,293 @@
+// The three passes as native chunk loops (replacing the Python chunk loops of the reference's
+// ThreePassMLIAP.compute_forces, mace_onegpu/mliap_threepass.py:504-587), plus the library's error plumbing.
+//
+// Per chunk [a, b) of receivers (nC = b - a) with per-chunk scratch of the eval struct:
+//   pass A:  msg1, rho1 = edge_l1_fwd;  x1 = msg1 M0[s] / (rho1 + 1);  A1 = symcon1(x1);  H1[a:b] = A1 Wp1
+//   pass B:  sc = h1_0e Wsk1[s];  msg2, rho2 = edge_l2_fwd(X2);  x2 = lin2(msg2) / (rho2 + 1);  A2 = symcon2(x2);
+//            h2 = sc + A2 Wp2;  e2, g_h2 = readout2;  gA2 = g_h2 Wp2^T;  G1[a:b]_0e += g_h2 Wsk1[s]^T;
+//            g_x2, g_rho2 = symcon2^T;  g_msg2 = g_x2 lin2^T / (rho2 + 1);  PF, GX2 += edge_l2_bwd
+//            (after all chunks: G1 += GX2 Wup2^T)
+//   pass C:  msg1, rho1, x1 as pass A;  g_h1 = G1r[a:b] + scale wr0;  gA1 = g_h1 Wp1^T;  g_x1, g_rho1 = symcon1^T;
+//            g_msg1 = g_x1 M0[s]^T / (rho1 + 1);  PF += edge_l1_bwd
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+#include "tp_gen.cuh"
+
+namespace mb {
+
+static thread_local char g_err[512] = "";
+static unsigned long long g_launches = 0;       // kernels launched by this library (all threads)
+
+// Optional per-kind CUDA-event timing of the pass runners (enabled by mace_b200_timing(1, ...)).
+struct KindTimer {
+  bool on = false;
+  cudaEvent_t ev[2][8192];
+  int kind[8192];
+  int n = 0;
+  double ms[MB_NKINDS] = {0};
+  long long cnt[MB_NKINDS] = {0};
+};
+static KindTimer g_tm;
+static bool g_tm_init = false;
+
+void timer_begin(int kind, cudaStream_t st, int* slot) {
+  *slot = -1;
+  if (!g_tm.on || g_tm.n >= 8192) return;
+  *slot = g_tm.n++;
+  g_tm.kind[*slot] = kind;
+  cudaEventRecord(g_tm.ev[0][*slot], st);
+}
+
+void timer_end(int slot, cudaStream_t st) {
+  if (slot >= 0) cudaEventRecord(g_tm.ev[1][slot], st);
+}
+
+static void timer_flush() {
+  if (g_tm.n == 0) return;
+  cudaEventSynchronize(g_tm.ev[1][g_tm.n - 1]);
+  for (int q = 0; q < g_tm.n; ++q) {
+    float t = 0.f;
+    if (cudaEventElapsedTime(&t, g_tm.ev[0][q], g_tm.ev[1][q]) == cudaSuccess) {
+      g_tm.ms[g_tm.kind[q]] += t;
+      g_tm.cnt[g_tm.kind[q]] += 1;
+    }
+  }
+  g_tm.n = 0;
+}
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int check_launch(const char* what) {
+  __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return MB_E_CUDA;
+  }
+  return 0;
+}
+
+int gemm_launch(const float* X, int64_t ldx, const int32_t* xoff, int nseg, const float* B, float* Y, int64_t ldy,
+                int yoff, int mult, const int32_t* order, int n_atoms, const float* rho, int accumulate,
+                cudaStream_t st);
+int symcon_fwd(const mb_model_t* m, int block, const float* x, float* A, const int32_t* spec, int n, cudaStream_t st);
+int symcon_bwd(const mb_model_t* m, int block, const float* x, const float* gA, float* gx, const int32_t* spec,
+               const float* rho, float* grho, int n, cudaStream_t st);
+int readout2(const mb_model_t* m, const float* h2, double* eat, float* gh2, int n, cudaStream_t st);
+int readout1(const mb_model_t* m, const float* H1, double* eat, int n, cudaStream_t st);
+int gh1(const mb_model_t* m, const float* G1, float* out, int n, cudaStream_t st);
+int finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd, unsigned* fmax_bits,
+             cudaStream_t st);
+
+#define TIMED(kind, call)                 \
+  do {                                    \
+    int _slot;                            \
+    timer_begin((kind), st, &_slot);      \
+    int _rc = (call);                     \
+    timer_end(_slot, st);                 \
+    if (_rc) return _rc;                  \
+  } while (0)
+
+#define RC(x)                 \
+  do {                        \
+    int _rc = (x);            \
+    if (_rc) return _rc;      \
+  } while (0)
+
+static int check_pass_args(const mb_model_t* m, const mb_eval_t* ev, const char* who) {
+  if (!m || !ev || ev->nl < 0 || ev->nt < ev->nl || ev->chunk <= 0 || m->S <= 0 || m->C != MB_C) {
+    set_error("%s: bad model / eval arguments", who);
+    return MB_E_ARG;
+  }
+  if (ev->nl > 0 && (!ev->spec_off || !ev->order || !ev->s_msg || !ev->s_x || !ev->s_gx || !ev->s_a || !ev->s_ga ||
+                     !ev->s_h || !ev->s_gh || !ev->s_sc || !ev->s_rho || !ev->s_grho || !ev->H1 || !ev->rowptr)) {
+    set_error("%s: missing buffer", who);
+    return MB_E_ARG;
+  }
+  return 0;
+}
+
+static const int kOffL[2] = {0, 1};      // component offset of the 0e / 1o blocks of h1-like [4][C] rows
+
+// x1 = msg1 M0[s] / (rho1 + 1) for one chunk, species segment by segment
+static int x1_gemms(const mb_model_t* m, const mb_eval_t* ev, int a, int ci, cudaStream_t st) {
+  const int C = MB_C, S = m->S;
+  const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
+  for (int l = 0; l < 4; ++l) {
+    const int off = l * l;
+    for (int s = 0; s < S; ++s) {
+      const int n = so[s + 1] - so[s];
+      if (n <= 0) continue;
+      RC(gemm_launch(ev->s_msg, 16 * C, &off, 1, m->M0 + ((size_t)s * 4 + l) * C * C, ev->s_x, 16 * C, off,
+                     2 * l + 1, ev->order + a + so[s], n, ev->s_rho, 0, st));
+    }
+  }
+  return 0;
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int mace_b200_abi_version(void) { return MB_ABI_VERSION; }
+
+extern "C" int mace_b200_struct_sizes(int32_t* model_bytes, int32_t* eval_bytes) {
+  if (model_bytes) *model_bytes = (int32_t)sizeof(mb_model_t);
+  if (eval_bytes) *eval_bytes = (int32_t)sizeof(mb_eval_t);
+  return 0;
+}
+
+extern "C" unsigned long long mace_b200_launch_count(void) { return __atomic_load_n(&g_launches, __ATOMIC_RELAXED); }
+
+extern "C" int mace_b200_timing(int enable, double* ms_out, long long* count_out) {
+  if (!g_tm_init) {
+    for (int q = 0; q < 8192; ++q) {
+      if (cudaEventCreate(&g_tm.ev[0][q]) != cudaSuccess || cudaEventCreate(&g_tm.ev[1][q]) != cudaSuccess) {
+        set_error("timing: cudaEventCreate failed");
+        return MB_E_CUDA;
+      }
+    }
+    g_tm_init = true;
+  }
+  timer_flush();
+  if (ms_out)
+    for (int k = 0; k < MB_NKINDS; ++k) ms_out[k] = g_tm.ms[k];
+  if (count_out)
+    for (int k = 0; k < MB_NKINDS; ++k) count_out[k] = g_tm.cnt[k];
+  for (int k = 0; k < MB_NKINDS; ++k) {
+    g_tm.ms[k] = 0.0;
+    g_tm.cnt[k] = 0;
+  }
+  g_tm.on = enable != 0;
+  return 0;
+}
+extern "C" const char* mace_b200_last_error(void) { return g_err; }
+
+extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+  RC(check_pass_args(m, ev, "pass_a"));
+  cudaStream_t st = (cudaStream_t)stream;
+  const int C = MB_C;
+  for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
+    const int b = min(a + ev->chunk, ev->nl), nC = b - a;
+    TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
+    RC(x1_gemms(m, ev, a, ci, st));
+    TIMED(MB_K_SYMCON, symcon_fwd(m, 0, ev->s_x, ev->s_a, ev->spec + a, nC, st));
+    for (int l = 0; l < 2; ++l)
+      RC(gemm_launch(ev->s_a, 4 * C, &kOffL[l], 1, m->Wp1 + (size_t)l * C * C, ev->H1 + (size_t)a * 4 * C, 4 * C,
+                     kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0, st));
+  }
+  return readout1(m, ev->H1, ev->eat, ev->nl, st);
+}
+
+extern "C" int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+  RC(check_pass_args(m, ev, "x2_all"));
+  cudaStream_t st = (cudaStream_t)stream;
+  const int C = MB_C;
+  const size_t bytes = (size_t)ev->nt * 4 * C * sizeof(float);
+  if (cudaMemsetAsync(ev->G1, 0, bytes, st) != cudaSuccess || cudaMemsetAsync(ev->GX2, 0, bytes, st) != cudaSuccess) {
+    set_error("x2_all: cudaMemsetAsync failed");
+    return MB_E_CUDA;
+  }
+  for (int l = 0; l < 2; ++l)
+    RC(gemm_launch(ev->H1, 4 * C, &kOffL[l], 1, m->Wup2 + (size_t)l * C * C, ev->X2, 4 * C, kOffL[l], 2 * l + 1,
+                   nullptr, ev->nt, nullptr, 0, st));
+  return 0;
+}
+
+extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+  RC(check_pass_args(m, ev, "pass_b"));
+  cudaStream_t st = (cudaStream_t)stream;
+  const int C = MB_C, S = m->S;
+  if (ev->P > 0 && cudaMemsetAsync(ev->PF, 0, (size_t)ev->P * 3 * sizeof(float), st) != cudaSuccess) {
+    set_error("pass_b: cudaMemsetAsync(PF) failed");
+    return MB_E_CUDA;
+  }
+  const int zero = 0;
+  for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
+    const int b = min(a + ev->chunk, ev->nl), nC = b - a;
+    const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
+    // sc = skip_tp(h1_0e, species)
+    for (int s = 0; s < S; ++s) {
+      const int n = so[s + 1] - so[s];
+      if (n > 0)
+        RC(gemm_launch(ev->H1 + (size_t)a * 4 * C, 4 * C, &zero, 1, m->Wsk1 + (size_t)s * C * C, ev->s_sc, C, 0, 1,
+                       ev->order + a + so[s], n, nullptr, 0, st));
+    }
+    TIMED(MB_K_EDGE_L2_FWD, mace_b200_edge_l2_fwd(m, ev, a, b, st));
+    // x2 = linear(msg2) / (rho2 + 1), per output l over its mid copies
+    for (int l = 0; l < 4; ++l) {
+      int xoff[4];
+      for (int j = 0; j < TP2_GROUP_N[l]; ++j) xoff[j] = TP2_MID_OFF[TP2_GROUP_W0[l] + j];
+      RC(gemm_launch(ev->s_msg, TP2_NO * C, xoff, TP2_GROUP_N[l], m->Wlin2 + (size_t)TP2_GROUP_W0[l] * C * C,
+                     ev->s_x, 16 * C, l * l, 2 * l + 1, nullptr, nC, ev->s_rho, 0, st));
+    }
+    TIMED(MB_K_SYMCON, symcon_fwd(m, 1, ev->s_x, ev->s_a, ev->spec + a, nC, st));
+    RC(gemm_launch(ev->s_a, C, &zero, 1, m->Wp2, ev->s_sc, C, 0, 1, nullptr, nC, nullptr, 1, st));   // h2 in s_sc
+    RC(readout2(m, ev->s_sc, ev->eat + a, ev->s_gh, nC, st));
+    RC(gemm_launch(ev->s_gh, C, &zero, 1, m->Wp2T, ev->s_ga, C, 0, 1, nullptr, nC, nullptr, 0, st));
+    for (int s = 0; s < S; ++s) {
+      const int n = so[s + 1] - so[s];
+      if (n > 0)
+        RC(gemm_launch(ev->s_gh, C, &zero, 1, m->Wsk1T + (size_t)s * C * C, ev->G1 + (size_t)a * 4 * C, 4 * C, 0, 1,
+                       ev->order + a + so[s], n, nullptr, 1, st));
+    }
+    TIMED(MB_K_SYMCON, symcon_bwd(m, 1, ev->s_x, ev->s_ga, ev->s_gx, ev->spec + a, ev->s_rho, ev->s_grho, nC, st));
+    for (int l = 0; l < 4; ++l) {
+      const int off = l * l;
+      for (int j = 0; j < TP2_GROUP_N[l]; ++j) {
+        const int w = TP2_GROUP_W0[l] + j;
+        RC(gemm_launch(ev->s_gx, 16 * C, &off, 1, m->Wlin2T + (size_t)w * C * C, ev->s_msg, TP2_NO * C,
+                       TP2_MID_OFF[w], 2 * l + 1, nullptr, nC, ev->s_rho, 0, st));
+      }
+    }
+    TIMED(MB_K_EDGE_L2_BWD, mace_b200_edge_l2_bwd(m, ev, a, b, st));
+  }
+  for (int l = 0; l < 2; ++l)
+    RC(gemm_launch(ev->GX2, 4 * C, &kOffL[l], 1, m->Wup2T + (size_t)l * C * C, ev->G1, 4 * C, kOffL[l], 2 * l + 1,
+                   nullptr, ev->nt, nullptr, 1, st));
+  return 0;
+}
+
+extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+  RC(check_pass_args(m, ev, "pass_c"));
+  cudaStream_t st = (cudaStream_t)stream;
+  const int C = MB_C, S = m->S;
+  for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
+    const int b = min(a + ev->chunk, ev->nl), nC = b - a;
+    const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
+    TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
+    RC(x1_gemms(m, ev, a, ci, st));
+    RC(gh1(m, ev->G1 + (size_t)a * 4 * C, ev->s_a, nC, st));
+    for (int l = 0; l < 2; ++l)
+      RC(gemm_launch(ev->s_a, 4 * C, &kOffL[l], 1, m->Wp1T + (size_t)l * C * C, ev->s_ga, 4 * C, kOffL[l],
+                     2 * l + 1, nullptr, nC, nullptr, 0, st));
+    TIMED(MB_K_SYMCON, symcon_bwd(m, 0, ev->s_x, ev->s_ga, ev->s_gx, ev->spec + a, ev->s_rho, ev->s_grho, nC, st));
+    for (int l = 0; l < 4; ++l) {
+      const int off = l * l;
+      for (int s = 0; s < S; ++s) {
+        const int n = so[s + 1] - so[s];
+        if (n <= 0) continue;
+        RC(gemm_launch(ev->s_gx, 16 * C, &off, 1, m->M0T + ((size_t)s * 4 + l) * C * C, ev->s_msg, 16 * C, off,
+                       2 * l + 1, ev->order + a + so[s], n, ev->s_rho, 0, st));
+      }
+    }
+    TIMED(MB_K_EDGE_L1_BWD, mace_b200_edge_l1_bwd(m, ev, a, b, st));
+  }
+  return 0;
+}
+
+extern "C" int mace_b200_finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd,
+                                  uint32_t* fmax_bits, void* stream) {
+  if (!m || !ev || !PFd || !fmax_bits || !ev->PF || !ev->eat) {
+    set_error("finalize: bad arguments");
+    return MB_E_ARG;
+  }
+  return finalize(m, ev, perm, PFd, fmax_bits, (cudaStream_t)stream);
+}

@@ -1,0 +1,126 @@
+"""ctypes binding of libmace_b200.so (C ABI declared in include/mace_b200.h).
+
+The structs below mirror mb_model_t / mb_eval_t field by field.  The library is loaded once; a missing library is
+an error (there is no fallback implementation of any kernel).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libmace_b200.so")
+
+c_i32, c_i64, c_u32, c_u64, c_f32, c_f64 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64,
+                                            ctypes.c_float, ctypes.c_double)
+c_vp = ctypes.c_void_p
+
+
+class MBModel(ctypes.Structure):
+    _fields_ = [("C", c_i32), ("S", c_i32), ("M", c_i32),
+                ("r_lo", c_f32), ("inv_h", c_f32), ("r_max", c_f32), ("p_cut", c_f32), ("scale", c_f32),
+                ("tab1", c_vp), ("tab2", c_vp), ("wd1", c_vp), ("wd2", c_vp),
+                ("M0", c_vp), ("M0T", c_vp), ("Wp1", c_vp), ("Wp1T", c_vp), ("wr0", c_vp), ("sc1", c_vp),
+                ("Wup2", c_vp), ("Wup2T", c_vp), ("Wsk1", c_vp), ("Wsk1T", c_vp), ("Wlin2", c_vp), ("Wlin2T", c_vp),
+                ("sc2", c_vp), ("Wp2", c_vp), ("Wp2T", c_vp), ("W1r", c_vp), ("w2r", c_vp), ("e0", c_vp)]
+
+
+class MBEval(ctypes.Structure):
+    _fields_ = [("nl", c_i32), ("nt", c_i32), ("P", c_i64),
+                ("pair_i", c_vp), ("pair_j", c_vp), ("rij", c_vp), ("rowptr", c_vp), ("spec", c_vp),
+                ("H1", c_vp), ("X2", c_vp), ("G1", c_vp), ("GX2", c_vp), ("PF", c_vp), ("eat", c_vp),
+                ("chunk", c_i32), ("order", c_vp), ("spec_off", c_vp),
+                ("s_msg", c_vp), ("s_x", c_vp), ("s_gx", c_vp), ("s_a", c_vp), ("s_ga", c_vp), ("s_h", c_vp),
+                ("s_gh", c_vp), ("s_sc", c_vp), ("s_rho", c_vp), ("s_grho", c_vp), ("status", c_vp)]
+
+
+_SIGS = {
+    "mace_b200_abi_version": (c_i32, []),
+    "mace_b200_last_error": (ctypes.c_char_p, []),
+    "mace_b200_launch_count": (ctypes.c_ulonglong, []),
+    "mace_b200_struct_sizes": (c_i32, [ctypes.POINTER(c_i32), ctypes.POINTER(c_i32)]),
+    "mace_b200_timing": (c_i32, [c_i32, c_vp, c_vp]),
+    "mace_b200_ffma_peak": (c_i32, [c_i32, c_vp, c_vp, c_vp]),
+    "mace_b200_sc_layout": (c_i32, [c_i32, ctypes.POINTER(c_i32), ctypes.POINTER(c_u64)]),
+    "mace_b200_build_tables": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_f64, c_f64,
+                                       c_f64, c_vp, c_vp, c_vp, c_vp]),
+    "mace_b200_edge_l1_fwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_edge_l2_fwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_edge_l2_bwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_edge_l1_bwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_conv_tp_fwd": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_vp, c_vp,
+                                      c_i32, c_vp, c_i32, c_vp, c_vp]),
+    "mace_b200_conv_tp_bwd": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_vp, c_vp,
+                                      c_i32, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mace_b200_node_gemm": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp,
+                                    c_i32, c_vp]),
+    "mace_b200_symcon_fwd": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i32, c_vp]),
+    "mace_b200_symcon_bwd": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_vp]),
+    "mace_b200_pass_a": (c_i32, [c_vp, c_vp, c_vp]),
+    "mace_b200_x2_all": (c_i32, [c_vp, c_vp, c_vp]),
+    "mace_b200_pass_b": (c_i32, [c_vp, c_vp, c_vp]),
+    "mace_b200_pass_c": (c_i32, [c_vp, c_vp, c_vp]),
+    "mace_b200_finalize": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mace_b200_pack_rows": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp]),
+    "mace_b200_unpack_add_rows": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded library (raises if it was not built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python mace-million_b200/build.py` "
+                               "(the CUDA path has no fallback implementation)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        abi = L.mace_b200_abi_version()
+        if abi != 1:
+            raise RuntimeError(f"libmace_b200.so ABI {abi} != 1")
+        ms, es = c_i32(), c_i32()
+        L.mace_b200_struct_sizes(ctypes.byref(ms), ctypes.byref(es))
+        if (ms.value, es.value) != (ctypes.sizeof(MBModel), ctypes.sizeof(MBEval)):
+            raise RuntimeError(f"libmace_b200.so struct sizes {ms.value}/{es.value} do not match the binding "
+                               f"{ctypes.sizeof(MBModel)}/{ctypes.sizeof(MBEval)}")
+        _lib = L
+    return _lib
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().mace_b200_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({rc}): {msg}")
+
+
+def ptr(t) -> int | None:
+    """Device (or host) address of a tensor, None for None."""
+    return None if t is None else int(t.data_ptr())
+
+
+def byref(s):
+    return ctypes.byref(s)
+
+
+KINDS = ("edge_l1_fwd", "edge_l1_bwd", "edge_l2_fwd", "edge_l2_bwd", "symcon")
+
+
+def timing(enable: bool):
+    """Collect (and reset) the per-kind kernel timings; switch recording on/off.  Returns {kind: (ms, launches)}."""
+    ms = (ctypes.c_double * len(KINDS))()
+    cnt = (ctypes.c_longlong * len(KINDS))()
+    check(lib().mace_b200_timing(1 if enable else 0, ctypes.cast(ms, c_vp), ctypes.cast(cnt, c_vp)), "timing")
+    return {k: (ms[i], cnt[i]) for i, k in enumerate(KINDS)}
+
+
+def launch_count() -> int:
+    return int(lib().mace_b200_launch_count())

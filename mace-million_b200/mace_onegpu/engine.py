@@ -1,0 +1,290 @@
+"""Host side of the B200 three-pass force evaluation: folds the fp64 model into device buffers (mb_model_t), builds
+the per-call plan (receiver CSR, species-sorted chunk order) and runs the native passes (mb_eval_t) with the H1
+forward / G1 reverse halo exchanges between them.
+
+Folding (exact algebra, fp64 on the host, then fp32 on the device):
+* radial MLP constants folded into the matrices as in the reference's fused_radial.py:4-9
+  (A0 = W0/sqrt(8), A_k = cst W_k / sqrt(64));
+* layer-1 sender features X1 = linear_up(embedding(species)) depend only on the sender species, so they are folded
+  into the layer-1 spline table (T1 = W1 * X1[s_send]; the exactness argument of the reference's ace_layer1.py:2-16);
+* linear_1 and the species skip_tp of layer 1 commute with the per-receiver 1 / (rho + 1) and are folded into one
+  per-species, per-l matrix M0[s][l];
+* the symmetric contractions become per-(species, channel) monomial coefficients (o3.sc_entries order);
+* e3nn's 1 / sqrt(fan_in) and normalize2mom constants are folded into every matrix.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import numpy as np
+import torch
+
+from . import _native as N
+from . import model as Mdl
+from . import o3
+
+C = 128
+
+
+def _f32(t, device):
+    return torch.as_tensor(t, dtype=torch.float64).to(dtype=torch.float32, device=device).contiguous()
+
+
+def fold_weights(model: Mdl.MACEModel, cols) -> dict:
+    """All folded fp64 arrays (CPU numpy) for the species columns `cols` (model one-hot columns present)."""
+    a = model.arch
+    Zn = len(a.atomic_numbers)
+    S = len(cols)
+    P = {k: v.detach().double().numpy() for k, v in model.params().items()}
+    cst = Mdl.silu_normalize2mom_cst()
+    t1, t2 = Mdl.tp_tables()
+    out = {"S": S, "cst": cst}
+    for i in (0, 1):
+        Ws = [P[f"interactions.{i}.conv_tp_weights.{k}"] for k in range(4)]
+        out[f"A{i}"] = [Ws[0] / math.sqrt(Ws[0].shape[0])] + [cst * W / math.sqrt(W.shape[0]) for W in Ws[1:]]
+        out[f"wd{i}"] = P[f"interactions.{i}.density_fn.weight"] / math.sqrt(a.num_bessel)
+    emb = P["node_embedding.weight"][cols] / math.sqrt(Zn)                       # [S, C]
+    X1 = emb @ P["interactions.0.linear_up.weight"][0] / math.sqrt(C)             # [S, C]
+    out["X1"] = X1
+    cs = np.zeros((S * S, t1["nW"] * C))
+    for ss in range(S):
+        for sr in range(S):
+            cs[ss * S + sr] = np.tile(X1[ss], t1["nW"])
+    out["col_scale1"] = cs
+    Wl1 = P["interactions.0.linear.weight"]                                       # [4 mid entries, C, C]
+    Wsk0 = P["interactions.0.skip_tp.weight"]                                     # [4, C, Z, C]
+    M0 = np.zeros((S, 4, C, C))
+    for s, z in enumerate(cols):
+        for l in range(4):
+            (w,) = t1["lin_groups"][l]
+            M0[s, l] = (Wl1[w] / math.sqrt(C)) @ (Wsk0[l][:, z, :] / math.sqrt(C * Zn))
+    out["M0"] = M0
+    out["Wp1"] = P["products.0.linear.weight"] / math.sqrt(C)
+    out["wr0"] = P["readouts.0.weight"] / math.sqrt(C)
+    out["Wup2"] = P["interactions.1.linear_up.weight"] / math.sqrt(C)
+    out["Wsk1"] = np.stack([P["interactions.1.skip_tp.weight"][0][:, z, :] for z in cols]) / math.sqrt(C * Zn)
+    Wl2 = P["interactions.1.linear.weight"].copy()
+    for l, ws in t2["lin_groups"].items():
+        for w in ws:
+            Wl2[w] = Wl2[w] / math.sqrt(len(ws) * C)
+    out["Wlin2"] = Wl2
+    out["Wp2"] = P["products.1.linear.weight"][0] / math.sqrt(C)
+    out["W1r"] = P["readouts.1.linear_1.weight"] / math.sqrt(C)
+    out["w2r"] = cst * P["readouts.1.linear_2.weight"] / math.sqrt(a.readout_mlp)
+    out["e0"] = P["atomic_energies"][cols] + a.shift
+    for blk, prefix, Ls in ((0, "products.0", (0, 1)), (1, "products.1", (0,))):
+        ents = o3.sc_entries(Ls)
+        coef = np.zeros((S, len(ents), C))
+        for t, (L, M, nu, mono, row) in enumerate(ents):
+            W = P[f"{prefix}.sc.{L}.{nu}"]                                        # [Z, K, C]
+            coef[:, t, :] = np.einsum("k,skc->sc", row, W[cols])
+        out[f"sc{blk}"] = coef
+        out[f"sc{blk}_fp"] = o3.sc_fingerprint(ents)
+    return out
+
+
+class FoldedModel:
+    """Device-resident folded model for one species subset (the ctypes mb_model_t points into its tensors)."""
+
+    def __init__(self, model: Mdl.MACEModel, cols, spline_grid: int = 512, r_lo: float = 0.5, device="cuda"):
+        L = N.lib()
+        self.cols = [int(c) for c in cols]
+        self.device = torch.device(device)
+        a = model.arch
+        f = fold_weights(model, self.cols)
+        for blk in (0, 1):
+            n = N.c_i32()
+            fp = N.c_u64()
+            N.check(L.mace_b200_sc_layout(blk, N.byref(n), N.byref(fp)), "sc_layout")
+            if n.value != f[f"sc{blk}"].shape[1] or fp.value != f[f"sc{blk}_fp"]:
+                raise RuntimeError(f"symmetric contraction {blk}: library layout ({n.value}, {fp.value:#x}) does not match "
+                                   f"the host folding ({f[f'sc{blk}'].shape[1]}, {f[f'sc{blk}_fp']:#x}); "
+                                   "regenerate csrc/symcon_gen.cuh and rebuild")
+        S = f["S"]
+        self.S = S
+        self.M = int(spline_grid)
+        self.r_lo = float(r_lo)
+        self.r_max = float(a.r_max)
+        self.scale = float(a.scale)
+        self.folded = f
+        dev = self.device
+        t = {}
+        t["wd1"] = _f32(f["wd0"], dev)
+        t["wd2"] = _f32(f["wd1"], dev)
+        t["M0"] = _f32(f["M0"], dev)
+        t["M0T"] = _f32(np.ascontiguousarray(np.swapaxes(f["M0"], -1, -2)), dev)
+        t["Wp1"] = _f32(f["Wp1"], dev)
+        t["Wp1T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wp1"], -1, -2)), dev)
+        t["wr0"] = _f32(f["wr0"], dev)
+        t["sc1"] = _f32(f["sc0"], dev)
+        t["Wup2"] = _f32(f["Wup2"], dev)
+        t["Wup2T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wup2"], -1, -2)), dev)
+        t["Wsk1"] = _f32(f["Wsk1"], dev)
+        t["Wsk1T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wsk1"], -1, -2)), dev)
+        t["Wlin2"] = _f32(f["Wlin2"], dev)
+        t["Wlin2T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wlin2"], -1, -2)), dev)
+        t["sc2"] = _f32(f["sc1"], dev)
+        t["Wp2"] = _f32(f["Wp2"], dev)
+        t["Wp2T"] = _f32(np.ascontiguousarray(f["Wp2"].T), dev)
+        t["W1r"] = _f32(f["W1r"], dev)
+        t["w2r"] = _f32(f["w2r"], dev)
+        t["e0"] = torch.as_tensor(f["e0"], dtype=torch.float64, device=dev).contiguous()
+        # spline tables built on the GPU in fp64 (tab1 carries X1 of the sender species)
+        self.TV, self.TG = {}, {}
+        for i, key, D, csk in ((0, "tab1", 4 * C, "col_scale1"), (1, "tab2", 10 * C, None)):
+            A = [torch.as_tensor(x, dtype=torch.float64, device=dev).contiguous() for x in f[f"A{i}"]]
+            cs = None if csk is None else torch.as_tensor(f[csk], dtype=torch.float64, device=dev).contiguous()
+            TV = torch.empty(S * S, self.M, D, dtype=torch.float32, device=dev)
+            TG = torch.empty_like(TV)
+            cub = torch.empty(S * S, self.M - 1, D, 4, dtype=torch.float32, device=dev)
+            st = torch.cuda.current_stream(dev).cuda_stream
+            N.check(L.mace_b200_build_tables(N.ptr(A[0]), N.ptr(A[1]), N.ptr(A[2]), N.ptr(A[3]), A[0].shape[0],
+                                             A[0].shape[1], D, N.ptr(cs), S * S, self.M, self.r_lo, self.r_max,
+                                             float(a.num_poly_cutoff), N.ptr(TV), N.ptr(TG), N.ptr(cub), st),
+                    "build_tables")
+            t[key] = cub
+            self.TV[i], self.TG[i] = TV, TG
+            t[f"_A{i}"] = A
+        self.t = t
+        h = (self.r_max - self.r_lo) / (self.M - 1)
+        self.struct = N.MBModel(C=C, S=S, M=self.M, r_lo=self.r_lo, inv_h=1.0 / h, r_max=self.r_max,
+                                p_cut=float(a.num_poly_cutoff), scale=self.scale,
+                                **{k: N.ptr(v) for k, v in t.items() if not k.startswith("_")})
+
+
+class Plan:
+    """Per-call preparation: receiver-sorted pairs, CSR, compact species, species-sorted chunk order."""
+
+    def __init__(self, eng: "ThreePassEngine", pair_i, pair_j, rij, elems, nl: int, nt: int):
+        dev = eng.device
+        pi = torch.as_tensor(pair_i, device=dev).to(torch.int32)
+        pj = torch.as_tensor(pair_j, device=dev).to(torch.int32)
+        rij = torch.as_tensor(rij, device=dev).to(torch.float64)
+        self.P = int(pi.numel())
+        self.perm = None
+        if self.P > 1 and not bool((pi[1:] >= pi[:-1]).all()):
+            o = torch.argsort(pi, stable=True)
+            pi, pj, rij = pi[o], pj[o], rij[o]
+            self.perm = o.to(torch.int64).contiguous()
+        self.pi, self.pj, self.rij = pi.contiguous(), pj.contiguous(), rij.reshape(-1, 3).contiguous()
+        self.nl, self.nt = int(nl), int(nt)
+        self.rowptr = torch.searchsorted(pi, torch.arange(nl + 1, device=dev, dtype=torch.int32)).to(torch.int32)
+        el = torch.as_tensor(elems, device=dev).to(torch.int64)
+        spec = eng.col2s[el]
+        if bool((spec < 0).any()):
+            raise RuntimeError("Plan: an atom's species has no tables in this engine (rebuild it with that species)")
+        self.spec = spec.to(torch.int32).contiguous()
+        C_ = eng.chunk
+        S = eng.fm.S
+        nch = (nl + C_ - 1) // C_
+        cid = torch.arange(nl, device=dev) // C_
+        key = cid * S + self.spec[:nl].long()
+        og = torch.argsort(key, stable=True)
+        self.order = (og - cid[og] * C_).to(torch.int32).contiguous()
+        cnt = torch.bincount(key, minlength=max(nch * S, 1)).view(max(nch, 1), S).cpu().numpy()
+        off = np.zeros((max(nch, 1), S + 1), dtype=np.int32)
+        off[:, 1:] = np.cumsum(cnt, 1)
+        self.spec_off = np.ascontiguousarray(off.reshape(-1))
+        self.n_chunks = nch
+
+
+class ThreePassEngine:
+    """The three-pass evaluation on one GPU for a fixed model and species set."""
+
+    def __init__(self, model: Mdl.MACEModel, cols, chunk: int = 16384, spline_grid: int = 512, device="cuda"):
+        self.device = torch.device(device)
+        self.model = model
+        self.chunk = int(chunk)
+        self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device)
+        Zn = len(model.arch.atomic_numbers)
+        col2s = torch.full((Zn,), -1, dtype=torch.int64)
+        col2s[torch.as_tensor(self.fm.cols)] = torch.arange(len(self.fm.cols))
+        self.col2s = col2s.to(self.device)
+        self._buf = {}
+        self._cap = {}
+
+    # ------------------------------------------------------------------------------------------------ buffers
+    def _get(self, name, shape, dtype):
+        n = int(np.prod(shape))
+        b = self._buf.get(name)
+        if b is None or b.numel() < n or b.dtype != dtype:
+            b = torch.empty(max(n, 1), dtype=dtype, device=self.device)
+            self._buf[name] = b
+        return b[:n].view(*shape)
+
+    def plan(self, pair_i, pair_j, rij, elems, nl, nt) -> Plan:
+        return Plan(self, pair_i, pair_j, rij, elems, nl, nt)
+
+    def eval_struct(self, plan: Plan):
+        nl, nt, P, ch = plan.nl, plan.nt, plan.P, self.chunk
+        f32, f64 = torch.float32, torch.float64
+        b = dict(H1=self._get("H1", (nt, 4, C), f32), X2=self._get("X2", (nt, 4, C), f32),
+                 G1=self._get("G1", (nt, 4, C), f32), GX2=self._get("GX2", (nt, 4, C), f32),
+                 PF=self._get("PF", (P, 3), f32), eat=self._get("eat", (max(nl, 1),), f64),
+                 s_msg=self._get("s_msg", (ch, 40, C), f32), s_x=self._get("s_x", (ch, 16, C), f32),
+                 s_gx=self._get("s_gx", (ch, 16, C), f32), s_a=self._get("s_a", (ch, 4, C), f32),
+                 s_ga=self._get("s_ga", (ch, 4, C), f32), s_h=self._get("s_h", (ch, C), f32),
+                 s_gh=self._get("s_gh", (ch, C), f32), s_sc=self._get("s_sc", (ch, C), f32),
+                 s_rho=self._get("s_rho", (ch,), f32), s_grho=self._get("s_grho", (ch,), f32),
+                 status=self._get("status", (1,), torch.int32))
+        ev = N.MBEval(nl=nl, nt=nt, P=P, pair_i=N.ptr(plan.pi), pair_j=N.ptr(plan.pj), rij=N.ptr(plan.rij),
+                      rowptr=N.ptr(plan.rowptr), spec=N.ptr(plan.spec), chunk=ch, order=N.ptr(plan.order),
+                      spec_off=plan.spec_off.ctypes.data, **{k: N.ptr(v) for k, v in b.items()})
+        return ev, b
+
+    def _check_status(self, b, what):
+        s = int(b["status"].item())
+        if s:
+            names = [n for bit, n in ((1, "sender index out of range"), (2, "species out of range"),
+                                      (4, "bad CSR row pointer"), (8, "non-finite or zero edge vector"),
+                                      (16, "pair_i does not match its CSR row")) if s & bit]
+            raise RuntimeError(f"mace_b200 {what}: input error reported by the kernels: {', '.join(names)}")
+
+    # ------------------------------------------------------------------------------------------------ evaluation
+    def evaluate(self, plan: Plan, forward_exchange=None, reverse_exchange=None, check: bool = True):
+        """(eatoms fp64 [nl], pair forces dE/drij fp64 [P, 3] in the caller's pair order) on the device.
+        forward_exchange(H1 [nt, 512]) fills ghost rows from their owners; reverse_exchange(G1 [nt, 512]) adds
+        ghost rows onto their owners (both in place; None when nt == nl)."""
+        L = N.lib()
+        m = N.byref(self.fm.struct)
+        ev, b = self.eval_struct(plan)
+        evp = N.byref(ev)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        b["status"].zero_()
+        b["eat"].zero_()
+        N.check(L.mace_b200_pass_a(m, evp, st), "pass_a")
+        if forward_exchange is not None and plan.nt > plan.nl:
+            forward_exchange(b["H1"].view(plan.nt, 4 * C))
+        N.check(L.mace_b200_x2_all(m, evp, st), "x2_all")
+        N.check(L.mace_b200_pass_b(m, evp, st), "pass_b")
+        if reverse_exchange is not None and plan.nt > plan.nl:
+            reverse_exchange(b["G1"].view(plan.nt, 4 * C))
+        N.check(L.mace_b200_pass_c(m, evp, st), "pass_c")
+        PFd = self._get("PFd", (plan.P, 3), torch.float64)
+        fbits = self._get("fmax", (1,), torch.int32)
+        fbits.zero_()
+        N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
+        self._last = b
+        if check:
+            self._check_status(b, "evaluation")
+        self.fmax = float(fbits.view(torch.float32).item()) if check else None
+        return b["eat"][:plan.nl], PFd
+
+    def owner_exchange(self, owner, nl: int):
+        """Exchange callbacks for ghosts given by an owner map (owner[j] = local owner of atom j for j >= nl): the
+        single-process stand-in of LAMMPS' forward / reverse comm (mliap_threepass.py:40-55, 522, 556)."""
+        L = N.lib()
+        ghost = torch.as_tensor(owner, device=self.device)[nl:].to(torch.int32).contiguous()
+
+        def fwd(H):
+            st = torch.cuda.current_stream(self.device).cuda_stream
+            N.check(L.mace_b200_pack_rows(N.ptr(H), N.ptr(ghost), ghost.numel(), H.shape[1], N.ptr(H[nl:]), st),
+                    "pack_rows")
+
+        def rev(G):
+            st = torch.cuda.current_stream(self.device).cuda_stream
+            N.check(L.mace_b200_unpack_add_rows(N.ptr(G[nl:]), N.ptr(ghost), ghost.numel(), G.shape[1], N.ptr(G), st),
+                    "unpack_add_rows")
+
+        return fwd, rev

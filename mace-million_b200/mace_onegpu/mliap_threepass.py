@@ -1,0 +1,153 @@
+"""LAMMPS ML-IAP ("pair_style mliap unified <file.pt> 0") wrapper of the B200 three-pass MACE force evaluation.
+
+Drop-in for the reference's ``mace_onegpu.mliap_threepass.ThreePassMLIAP`` (mace_onegpu/mliap_threepass.py:155-622):
+same module path (pickles made with either resolve to this class), constructor signature, ML-IAP attributes,
+``compute_forces(data)`` contract (per-atom energies into data.eatoms, data.energy, pair forces dE/drij through
+data.update_pair_forces_gpu in the caller's pair order), H1 forward / G1 reverse exchange through
+data.forward_exchange / data.reverse_exchange with the same 2^31-element column split, the same guards
+(int32 neighbour-slot estimate, non-finite / absurd force abort) and the same MACE3P_* environment knobs that still
+mean something (CHUNK, LOG, SKIN, ALLOW_HUGE, FMAX_ABORT).
+
+Per call: pass A (layer-1 features of every local atom) -> forward exchange -> pass B (layer-2 energy, pair forces,
+G1 = dE2/dh1) -> reverse exchange -> pass C (loss E1 + G1 . h1, remaining pair forces); all arithmetic runs in the
+sm_100a kernels of libmace_b200.so (engine.py), there is no other implementation.
+"""
+from __future__ import annotations
+
+import json
+import os
+import time
+
+import torch
+
+try:
+    from lammps.mliap.mliap_unified_abc import MLIAPUnified
+except ImportError:  # pragma: no cover - LAMMPS is not part of this package
+    class MLIAPUnified:
+        def __init__(self):
+            pass
+
+_RUNTIME = ("_eng", "_dev", "_cols", "_log", "_fmax_abort", "_t_end")
+_INT_MAX = 2 ** 31 - 1
+
+
+def _exchange(fn, src, dst, D):
+    """LAMMPS' ML-IAP comm buffers are sized with 32-bit ints (ntotal * D): split the feature columns so that every
+    call stays below 2^31 elements (mace_onegpu/mliap_threepass.py:40-55)."""
+    nt = src.shape[0]
+    if nt * D < _INT_MAX:
+        fn(src, dst, D)
+        return
+    w = D
+    while nt * w >= _INT_MAX and w > 1:
+        w //= 2
+    for c in range(0, D, w):
+        cw = min(w, D - c)
+        s = src[:, c:c + cw].contiguous()
+        d = torch.empty_like(s)
+        fn(s, d, cw)
+        dst[:, c:c + cw] = d
+
+
+class ThreePassMLIAP(MLIAPUnified):
+    def __init__(self, model, chunk=16384, spline_grid=512, node_bucket=8192, e_align=65536, rebuild_config=None):
+        super().__init__()
+        from .model import CHEMICAL_SYMBOLS
+
+        self.model = model
+        self.element_types = [CHEMICAL_SYMBOLS[int(z)] for z in model.atomic_numbers]
+        self.num_species = len(self.element_types)
+        self.rcutfac = 0.5 * float(model.r_max)
+        self.ndescriptors = 1
+        self.nparams = 1
+        self.chunk = int(chunk)
+        self.spline_grid = int(spline_grid)
+        # node_bucket / e_align pad the reference's cuEquivariance shapes; the B200 kernels need no padding
+        self.node_bucket = int(node_bucket)
+        self.e_align = int(e_align)
+        self.dtype = torch.float32
+        self.step = 0
+        self._rebuild = None
+
+    def __getstate__(self):
+        d = self.__dict__.copy()
+        for k in _RUNTIME:
+            d.pop(k, None)
+        return d
+
+    # ------------------------------------------------------------------------------------------------ setup
+    def _setup(self, elems):
+        from .engine import ThreePassEngine
+
+        dev = elems.device if elems.is_cuda else torch.device("cuda", torch.cuda.current_device())
+        self._dev = dev
+        if os.environ.get("MACE3P_CHUNK"):
+            self.chunk = int(os.environ["MACE3P_CHUNK"])
+        cols = sorted(int(c) for c in torch.unique(elems).tolist())
+        self._cols = cols
+        self._eng = ThreePassEngine(self.model, cols, chunk=self.chunk, spline_grid=self.spline_grid or 512,
+                                    device=dev)
+        self._fmax_abort = float(os.environ.get("MACE3P_FMAX_ABORT", "100.0"))
+        path = os.environ.get("MACE3P_LOG")
+        self._log = open(path, "a", buffering=1) if path else None
+
+    # ------------------------------------------------------------------------------------------------ entry point
+    def compute_forces(self, data):
+        nl, nt, P = int(data.nlocal), int(data.ntotal), int(data.npairs)
+        if nl == 0 or P <= 1:
+            return
+        t_start = time.perf_counter()
+        t_gap = (t_start - self._t_end) if getattr(self, "_t_end", None) else None
+        # int32 guard of the Kokkos neighbour list (mliap_threepass.py:450-461)
+        skin = float(os.environ.get("MACE3P_SKIN", "2.0"))
+        rmax = 2.0 * self.rcutfac
+        est_slots = P * ((rmax + skin) / rmax) ** 3
+        if est_slots > 0.95 * 2 ** 31 and os.environ.get("MACE3P_ALLOW_HUGE", "0") != "1":
+            raise RuntimeError(f"ThreePassMLIAP guard: nlocal={nl:,}, pairs={P:,} -> estimated LAMMPS neighbour slots "
+                               f"{est_slots:.3e} is close to the 2^31 int32 limit of the Kokkos neighbour list "
+                               f"(skin {skin} A). Use fewer atoms per GPU, a smaller skin, or more GPUs.")
+        elems = torch.as_tensor(data.elems).long()
+        if not hasattr(self, "_eng") or not set(torch.unique(elems).tolist()) <= set(self._cols):
+            self._setup(elems)
+        self.step += 1
+        eng = self._eng
+        dev = self._dev
+        pi = torch.as_tensor(data.pair_i).to(dev, non_blocking=True)
+        pj = torch.as_tensor(data.pair_j).to(dev, non_blocking=True)
+        rij = torch.as_tensor(data.rij).to(dev, non_blocking=True)
+        plan = eng.plan(pi, pj, rij, elems.to(dev, non_blocking=True), nl, nt)
+        D = 512
+
+        def fwd(H):
+            tmp = torch.empty_like(H)
+            _exchange(data.forward_exchange, H, tmp, D)
+            H.copy_(tmp)
+
+        def rev(G):
+            tmp = torch.empty_like(G)
+            _exchange(data.reverse_exchange, G, tmp, D)
+            G.copy_(tmp)
+
+        eat, PF = eng.evaluate(plan, fwd if nt > nl else None, rev if nt > nl else None)
+        fmax = eng.fmax
+        # force guard (mliap_threepass.py:595-601)
+        if not (bool(torch.isfinite(eat).all()) and fmax == fmax and fmax < self._fmax_abort):
+            raise RuntimeError(f"ThreePassMLIAP guard: non-finite or absurd output at call {self.step} "
+                               f"(max |pair force| = {fmax:.3e} eV/A, limit {self._fmax_abort:g}); aborting before LAMMPS "
+                               f"integrates it. The model is probably extrapolating (check the trajectory / training data).")
+        torch.as_tensor(data.eatoms).copy_(eat)
+        data.energy = float(eat.sum())
+        data.update_pair_forces_gpu(PF)
+        if self._log is not None:
+            torch.cuda.synchronize()
+            self._log.write(json.dumps(dict(step=self.step, nlocal=nl, ntotal=nt, npairs=P,
+                                            chunks=(nl + self.chunk - 1) // self.chunk,
+                                            sorted_pairs=plan.perm is None, t_total=time.perf_counter() - t_start,
+                                            t_gap_lammps=t_gap, fmax=fmax)) + "\n")
+        self._t_end = time.perf_counter()
+
+    def compute_descriptors(self, data):
+        pass
+
+    def compute_gradients(self, data):
+        pass

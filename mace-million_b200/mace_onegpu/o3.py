@@ -275,3 +275,30 @@ def sc_monomial_form(nu: int, L: int, lmax: int = LMAX_SH):
     if not keep:
         return [], np.zeros((2 * L + 1, 0, K))
     return keep, np.stack(rows, axis=1)
+
+
+# ----------------------------------------------------------------------------------------------- coefficient layout
+def sc_entries(Ls, lmax: int = LMAX_SH, correlation: int = 3):
+    """Canonical order of the per-(species, channel) coefficients of a symmetric contraction with outputs Ls:
+    for L in Ls, nu = 1..correlation, monomial (sorted indices, combinations order), output component M.
+    Returns [(L, M, nu, mono, row)] where row [K_{L,nu}] maps the contraction weights w[k] to the coefficient."""
+    out = []
+    for L in Ls:
+        for nu in range(1, correlation + 1):
+            monos, Us = sc_monomial_form(nu, L, lmax)
+            for a, mono in enumerate(monos):
+                for M in range(2 * L + 1):
+                    row = Us[M, a]
+                    if np.abs(row).max() > 1e-12:
+                        out.append((L, M, nu, tuple(mono), row))
+    return out
+
+
+def sc_fingerprint(entries) -> int:
+    """FNV-1a 64-bit hash of the entry order (L, M, nu, mono) shared by the host folding and the generated kernels."""
+    h = 0xCBF29CE484222325
+    for (L, M, nu, mono, _row) in entries:
+        for v in (L, M, nu, *mono, 255):
+            h ^= int(v) & 0xFF
+            h = (h * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return h

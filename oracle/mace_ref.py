@@ -265,8 +265,9 @@ class MaceRef:
         return eat.detach(), gv.detach()
 
     # ------------------------------------------------------------------------------------------ three pass
-    def three_pass(self, pi, pj, rij, elems, nl, chunk, owner=None):
-        """The receiver-chunked three-pass evaluation with ML-IAP semantics; returns (eatoms [nl], PF [P, 3])."""
+    def three_pass(self, pi, pj, rij, elems, nl, chunk, owner=None, return_state=False):
+        """The receiver-chunked three-pass evaluation with ML-IAP semantics; returns (eatoms [nl], PF [P, 3]) and,
+        with return_state, also H1 [nt, C, 4] after the forward exchange and G1r [nl, C, 4] after the reverse one."""
         pi, pj = torch.as_tensor(pi).long(), torch.as_tensor(pj).long()
         elems = torch.as_tensor(elems).long()
         nt = elems.numel()
@@ -315,6 +316,8 @@ class MaceRef:
             (gv,) = torch.autograd.grad(loss, [vec])
             PF[order[e0:e1]] += gv
             eat[a:b] += self.scale * R1.detach()
+        if return_state:
+            return eat, PF, H1, G1r
         return eat, PF
 
     def _chunk_l1(self, a, b, e0, e1, pi_s, pj_s, rij_s, elems, vec):
