@@ -135,6 +135,18 @@ int mace_b200_build_tables(const double* A0, const double* A1, const double* A2,
                            double r_lo, double r_max, double p_cut, float* TV, float* TG, float* cubic,
                            void* stream);
 
+/* Allocation-free variant of mace_b200_build_tables (no counterpart in the reference).  For callers that must not
+ * have the library allocate device memory (an MD engine that owns all device memory through its own pool, or a
+ * process with a fixed device footprint): same arguments and outputs, but the fp64 sample scratch is a static device
+ * array of the library, so M * D is limited to 512 * 1280 (15 MiB, held by every GPU that loads the library until
+ * exit); larger tables are rejected with MB_E_ARG.  It calls no cudaMalloc / cudaFree.  The first call on a device
+ * resolves the scratch's device address (cudaGetSymbolAddress) with that device current: make that first call
+ * before any stream capture.  All calls share the scratch, so calls that overlap on the GPU race: serialise them. */
+int mace_b200_build_tables_noalloc(const double* A0, const double* A1, const double* A2, const double* A3,
+                                   int32_t n_in, int32_t hidden, int32_t D, const double* col_scale, int32_t n_pairs,
+                                   int32_t M, double r_lo, double r_max, double p_cut, float* TV, float* TG,
+                                   float* cubic, void* stream);
+
 /* ---------------------------------------------------------------- edge kernels (one receiver chunk [a, b))
  * edge_l1_fwd replaces ConvSpline.forward (mace_onegpu/conv_spline.py:294-301) and the density sum
  *   (fast_layers.py:179-183): s_msg[i][lm][c] = sum_e T1(r_e, p_e)[l][c] Y_e[lm], s_rho[i] = sum_e tanh(d_e^2).

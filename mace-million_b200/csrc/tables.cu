@@ -110,3 +110,66 @@ extern "C" int mace_b200_build_tables(const double* A0, const double* A1, const 
   cudaFreeAsync(smp, st);
   return rc;
 }
+
+// ------------------------------------------------------------------------------------------------ allocation-free
+// Some callers cannot allocate device memory when they (re)build tables: an MD engine that owns all device memory
+// through its own pool (LAMMPS/Kokkos builds) and must not have a library allocate behind its back, or a process that
+// caps its device footprint after start-up.  mace_b200_build_tables_noalloc serves them: it runs the same two kernels
+// as mace_b200_build_tables, but its fp64 sample scratch is this file-scope device array instead of a
+// cudaMallocAsync buffer.  Capacity: M * D <= 512 * 1280 (the largest table of the MACE-MPA-0 architecture at the
+// default 512-knot grid), i.e. 3 * 655,360 doubles = 15 MiB, held by every GPU that loads the library until exit.
+#include <mutex>
+
+static constexpr size_t kNoAllocMD = 512 * 1280;
+static __device__ __align__(256) double g_noalloc_samples[3 * kNoAllocMD];
+
+static std::mutex g_noalloc_mu;
+static constexpr int kMaxDevices = 64;
+static double* g_noalloc_ptr[kMaxDevices] = {nullptr};   // device address of g_noalloc_samples, per device ordinal
+
+extern "C" int mace_b200_build_tables_noalloc(const double* A0, const double* A1, const double* A2, const double* A3,
+                                              int32_t n_in, int32_t hidden, int32_t D, const double* col_scale,
+                                              int32_t n_pairs, int32_t M, double r_lo, double r_max, double p_cut,
+                                              float* TV, float* TG, float* cubic, void* stream) {
+  if (!A0 || !A1 || !A2 || !A3 || n_in <= 0 || n_in > 64 || hidden <= 0 || hidden > 1024 || D <= 0 || n_pairs <= 0 ||
+      M < 2 || !(r_max > r_lo) || r_lo <= 0.0) {
+    set_error("build_tables_noalloc: bad arguments");
+    return MB_E_ARG;
+  }
+  if ((size_t)M * (size_t)D > kNoAllocMD) {
+    set_error("build_tables_noalloc: M * D = %lld exceeds the static scratch capacity %zu (at most 512 knots x 1280 "
+              "columns); use mace_b200_build_tables", (long long)M * D, kNoAllocMD);
+    return MB_E_ARG;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("build_tables_noalloc: no usable current device");
+    return MB_E_CUDA;
+  }
+  double* smp = nullptr;
+  {
+    // first call on this device: resolve the device address of the static scratch (the symbol itself is only a
+    // host-side stand-in); host code must never hand the symbol to a kernel.
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      cudaError_t e = cudaGetSymbolAddress((void**)&g_noalloc_ptr[dev], g_noalloc_samples);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        set_error("build_tables_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        return MB_E_CUDA;
+      }
+    }
+    smp = g_noalloc_ptr[dev];
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const double h = (r_max - r_lo) / (M - 1);
+  const double eps = 1e-5 * (r_max - r_lo);
+  // k_sample_mlp writes every [s][k][d] entry of the scratch before k_finish_tables reads it: nothing has to start at
+  // zero.  Calls that overlap on the GPU (other streams) share this scratch and race; serialise them.
+  size_t shm = sizeof(double) * (n_in + 2 * hidden);
+  k_sample_mlp<<<dim3(M, 3), 128, shm, st>>>(A0, A1, A2, A3, n_in, hidden, D, M, r_lo, h, eps, r_max, p_cut, smp);
+  int rc = check_launch("k_sample_mlp");
+  if (rc) return rc;
+  k_finish_tables<<<1184, 256, 0, st>>>(smp, col_scale, n_pairs, M, D, h, eps, TV, TG, (float4*)cubic);
+  return check_launch("k_finish_tables");
+}

@@ -44,6 +44,8 @@ _SIGS = {
     "mace_b200_sc_layout": (c_i32, [c_i32, ctypes.POINTER(c_i32), ctypes.POINTER(c_u64)]),
     "mace_b200_build_tables": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_f64, c_f64,
                                        c_f64, c_vp, c_vp, c_vp, c_vp]),
+    "mace_b200_build_tables_noalloc": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_f64,
+                                               c_f64, c_f64, c_vp, c_vp, c_vp, c_vp]),
     "mace_b200_edge_l1_fwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
     "mace_b200_edge_l2_fwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
     "mace_b200_edge_l2_bwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
