@@ -11,7 +11,10 @@ inputs already resident in HBM (the pair list is 2.2 GB of fp64 vectors, larger 
 copies of the pair list and the device->host copies of energies and pair forces inside the timed region.
 `--impl reference` times the CPU fp64 restatement of the reference's algorithm (oracle/, the reference itself cannot
 be installed: mace-torch / e3nn / cuEquivariance are absent) on a bounded sample of the same workload.
-Multi-GPU (torchrun): each rank evaluates its own copy of the configuration (weak scaling).
+Multi-GPU (torchrun, one rank per GPU): spatial domain decomposition of the periodic box (2x1x1, 2x2x1, 2x2x2 blocks)
+with explicit ghost atoms (shell r_max + 2 A skin) and the H1 forward / G1 reverse halo exchanges as NCCL grouped
+send/recv inside every timed step.  --scaling weak (default) keeps 1.03M atoms per GPU (the global box grows with N,
+BASELINE config 5 at N = 8); --scaling strong splits the 1.03M-atom box over the N GPUs.
 """
 from __future__ import annotations
 
@@ -60,14 +63,18 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=6, help="water molecules per box edge of the CPU sample")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--skin", type=float, default=2.0, help="ghost shell = r_max + skin (multi-GPU)")
     return ap.parse_args()
 
 
-def build_structure(cfg):
+def build_structure(cfg, grid=(1, 1, 1)):
     from mace_onegpu import structures as S
 
     if cfg["kind"] == "water":
-        return S.water_box(cfg["n"], seed=cfg["seed"])
+        return S.water_box(cfg["n"] * grid[0], cfg["n"] * grid[1], cfg["n"] * grid[2], seed=cfg["seed"])
+    if tuple(grid) != (1, 1, 1):
+        raise ValueError("weak scaling is defined for the water boxes")
     return S.alloy_bcc(cfg["n"], seed=cfg["seed"])
 
 
@@ -203,17 +210,40 @@ def main():
     from mace_onegpu.mliap_threepass import ThreePassMLIAP
 
     m = M.default_model(cfg["model_seed"])
-    pos, Z, box = build_structure(cfg)
-    cols = torch.as_tensor(S.species_columns(Z, m.arch.atomic_numbers))
-    pi, pj, rij = NB.neighbor_list(pos, box, m.arch.r_max, device=dev)
-    n = len(Z)
+    hx = None
+    if world == 1:
+        pos, Z, box = build_structure(cfg)
+        cols_all = torch.as_tensor(S.species_columns(Z, m.arch.atomic_numbers))
+        pi, pj, rij = NB.neighbor_list(pos, box, m.arch.r_max, device=dev)
+        n = nt = len(Z)
+        cols = cols_all
+        parallelism = "single"
+    else:
+        from mace_onegpu import domain as DM
+
+        grid = DM.grid_for(world)
+        pos, Z, box = build_structure(cfg, grid if args.scaling == "weak" else (1, 1, 1))
+        cols_all = torch.as_tensor(S.species_columns(Z, m.arch.atomic_numbers))
+        dec = DM.Decomposition(pos, box, grid, m.arch.r_max + args.skin)
+        p, gid, n = dec.rank_atoms(rank)
+        nt = len(gid)
+        pi, pj, rij = NB.neighbor_list_open(p, n, m.arch.r_max, device=dev)
+        cols = cols_all[torch.as_tensor(gid)]
+        hx = DM.HaloExchange(dec, rank, dev)
+        parallelism = f"domain {grid[0]}x{grid[1]}x{grid[2]}, NCCL halo exchange, ghost shell {m.arch.r_max + args.skin:g} A"
     P = int(pi.numel())
     elems = cols.to(dev)
-    eng = ThreePassEngine(m, sorted(set(cols.tolist())), chunk=args.chunk, device=dev)
+    eng = ThreePassEngine(m, sorted(set(cols_all.tolist())), chunk=args.chunk, device=dev)
+    n_all = torch.tensor([n], device=dev, dtype=torch.int64)
+    if world > 1:
+        dist.all_reduce(n_all)
+    n_total = int(n_all.item())
 
     def step():
-        plan = eng.plan(pi, pj, rij, elems, n, n)
-        return eng.evaluate(plan)
+        plan = eng.plan(pi, pj, rij, elems, n, nt)
+        if hx is None:
+            return eng.evaluate(plan)
+        return eng.evaluate(plan, hx.forward, hx.reverse)
 
     for _ in range(args.warmup):
         step()
@@ -241,7 +271,7 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
     ms_per_step = ms / args.steps
-    value = n * world * args.steps / (ms * 1e-3)
+    value = n_total * args.steps / (ms * 1e-3)
 
     # roofline of the dominant kernel (FP32 SIMT edge kernels: FLOP/s against the measured FFMA issue ceiling)
     dom = max((k for k in kern if k in FLOPS_PER_EDGE), key=lambda k: kern[k][0])
@@ -262,7 +292,7 @@ def main():
         hpj = pj.cpu().pin_memory()
         hrij = rij.cpu().pin_memory()
         hel = cols.clone().pin_memory()
-        data = MLIAPData(hpi, hpj, hrij, hel, n, host_outputs=True)
+        data = MLIAPData(hpi, hpj, hrij, hel, n, host_outputs=True, exchange=hx)
         for _ in range(max(1, args.warmup)):
             mli.compute_forces(data)
         torch.cuda.synchronize()
@@ -279,8 +309,8 @@ def main():
             tt = torch.tensor([ems], device=dev, dtype=torch.float64)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ems = float(tt.item())
-        e2e = {"value": n * world * args.steps / (ems * 1e-3), "unit": "atoms/s",
-               "h2d_bytes_per_step": int(P * (4 + 4 + 24) + n * 8), "d2h_bytes_per_step": int(n * 8 + P * 24)}
+        e2e = {"value": n_total * args.steps / (ems * 1e-3), "unit": "atoms/s",
+               "h2d_bytes_per_step": int(P * (4 + 4 + 24) + nt * 8), "d2h_bytes_per_step": int(n * 8 + P * 24)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -292,11 +322,14 @@ def main():
     if rank == 0:
         kinds = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps} for k, v in kern.items()}
         line = {"metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": args.scaling if world > 1 else "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": args.config, "description": cfg["desc"], "atoms_per_gpu": n, "pairs_per_gpu": P,
-                           "chunk": args.chunk, "spline_knots": 512, "model": "MACE-MPA-0-medium architecture, random init",
-                           "parallelism": "replicas" if world > 1 else "single", "l2": "inputs larger than L2 (no flush)"},
+                "config": {"workload": args.config, "description": cfg["desc"], "atoms_total": n_total,
+                           "atoms_rank0": n, "ghosts_rank0": nt - n, "pairs_rank0": P, "chunk": args.chunk,
+                           "spline_knots": 512, "model": "MACE-MPA-0-medium architecture, random init",
+                           "parallelism": parallelism, "gemm": "tcgen05 3xTF32" if eng.fm.use_tc else "SIMT fp32",
+                           "l2": "inputs larger than L2 (no flush)"},
                 "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak, "traffic": None,
                              "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",

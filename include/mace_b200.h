@@ -39,6 +39,7 @@ enum {
   MB_ST_BAD_ROWPTR = 4,
   MB_ST_NONFINITE = 8,
   MB_ST_BAD_RECEIVER = 16,
+  MB_ST_TC_TIMEOUT = 32,      /* a tensor-core kernel gave up waiting on its MMA barrier (bounded wait) */
 };
 
 /* Folded, device-resident model (fp32 unless noted).  S = number of species present (compact indices),
@@ -69,6 +70,21 @@ typedef struct {
   const float* W1r;            /* [C][16]       readouts[1].linear_1 / sqrt(C) */
   const float* w2r;            /* [16]          readouts[1].linear_2 * cst / sqrt(16) */
   const double* e0;            /* [S]           E0 + shift per species (fp64) */
+  /* tensor-core copies: the K-major form of each matrix above used as a GEMM B operand (X_tc = transpose of X),
+   * split into two planes [2][...] of tf32-rounded hi and lo parts (3xTF32); used when use_tc != 0 */
+  const float* M0_tc;
+  const float* M0T_tc;
+  const float* Wp1_tc;
+  const float* Wp1T_tc;
+  const float* Wup2_tc;
+  const float* Wup2T_tc;
+  const float* Wsk1_tc;
+  const float* Wsk1T_tc;
+  const float* Wlin2_tc;
+  const float* Wlin2T_tc;
+  const float* Wp2_tc;
+  const float* Wp2T_tc;
+  int32_t use_tc;              /* node GEMMs on tcgen05 (3xTF32) instead of the SIMT fp32 kernel */
 } mb_model_t;
 
 /* One force evaluation: the pair list (receiver-sorted), persistent per-atom state and per-chunk scratch. */
@@ -185,6 +201,13 @@ int mace_b200_conv_tp_bwd(const float* X, int32_t nX, const float* Y, int32_t nY
 int mace_b200_node_gemm(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg, const float* B,
                         float* Y, int64_t ldy, int32_t yoff, int32_t mult, const int32_t* order, int32_t n_atoms,
                         const float* rho, int32_t accumulate, void* stream);
+
+/* The same GEMM on the 5th-generation tensor cores (tcgen05.mma kind::tf32, accumulator in TMEM), 3xTF32:
+ * Bt_split = [2][n_seg][128 n][128 k] (K-major B, tf32 hi plane then lo plane, plane = elements per plane).
+ * A timeout of its bounded MMA-barrier wait sets MB_ST_TC_TIMEOUT in *status (may be null). */
+int mace_b200_node_gemm_tc(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg, const float* Bt_split,
+                           int64_t plane, float* Y, int64_t ldy, int32_t yoff, int32_t mult, const int32_t* order,
+                           int32_t n_atoms, const float* rho, int32_t accumulate, uint32_t* status, void* stream);
 
 /* ---------------------------------------------------------------- symmetric contraction
  * Replaces products[k].symmetric_contractions (mace EquivariantProductBasisBlock, correlation 3).

@@ -21,6 +21,7 @@ enum : unsigned {
   ST_NONFINITE = 1u << 3,      // non-finite edge vector
   ST_BAD_RECEIVER = 1u << 4,   // pair_i does not match the CSR row
 };
+#define MB_ST_TC_TIMEOUT (1u << 5)  // a tensor-core kernel gave up waiting on its MMA barrier
 
 __device__ __forceinline__ void set_status(unsigned* st, unsigned bit) {
   if (st) atomicOr(st, bit);

@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(128) k_edge_l1_bwd(const mb_model_t m, const m
 // s_msg[i][o][c] = sum_e sum_t coef_t W2(r_e)[w_t][c] X2[j_e][k_t][c] Y_e[m_t];  s_rho[i]
 template <int EB>
 __global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
-  __shared__ float scy[EB][TP2_NT];
+  __shared__ __align__(16) float scy[EB][TP2_NT_PAD];
   __shared__ int srow[EB];
   __shared__ int ssend[EB];
   __shared__ float st[EB];
@@ -319,10 +319,12 @@ __global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const m
 
 // ------------------------------------------------------------------------------------------------ layer 2 backward
 // Pass B: given g = dE/dmsg2 (s_msg, [i][40][C]) and s_grho: PF[e] += dE/dv_e, GX2[j_e] += dE/dX2.
+// Per receiver and channel the products cg = coef * g[o] live in registers (tp2_cg); per edge the 16 SH values are
+// read once from shared memory.
 template <int EB>
 __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const mb_eval_t ev, int a) {
-  __shared__ float scy[EB][TP2_NT];
-  __shared__ float sJ[EB][48];
+  __shared__ __align__(16) float sY[EB][16];
+  __shared__ __align__(16) float sJ[EB][48];
   __shared__ float su[EB][3];
   __shared__ float sgd[EB];
   __shared__ int srow[EB];
@@ -334,10 +336,11 @@ __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const m
   int64_t e0, e1;
   if (!row_range(ev, i, e0, e1)) return;
   const float4* tab = reinterpret_cast<const float4*>(m.tab2);
-  float g[TP2_NO];
+  float g[TP2_NO], cg[TP2_NCG];
   const float* gin = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;
 #pragma unroll
   for (int q = 0; q < TP2_NO; ++q) g[q] = gin[q * MB_C];
+  tp2_cg(g, cg);
   const float grho = ev.s_grho[il];
   for (int64_t base = e0; base < e1; base += EB) {
     const int n = (int)min((int64_t)EB, e1 - base);
@@ -356,9 +359,7 @@ __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const m
         ssend[c] = j;
         const float ir = 1.f / r;
         float3 u = make_float3(v.x * ir, v.y * ir, v.z * ir);
-        float Y[16];
-        sh_jacobian(u, r, Y, sJ[c]);
-        tp2_cy(Y, scy[c]);
+        sh_jacobian(u, r, sY[c], sJ[c]);
         su[c][0] = u.x;
         su[c][1] = u.y;
         su[c][2] = u.z;
@@ -374,13 +375,20 @@ __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const m
       if (row < 0) continue;
       const int j = ssend[q];
       const float* xs = ev.X2 + (size_t)j * 4 * MB_C + c;
-      float X[4], gX[4] = {0.f, 0.f, 0.f, 0.f}, gY[16];
+      float X[4], gX[4] = {0.f, 0.f, 0.f, 0.f}, gY[16], Y[16];
 #pragma unroll
       for (int k = 0; k < 4; ++k) X[k] = __ldg(xs + k * MB_C);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) gY[k] = 0.f;
+      for (int k = 0; k < 16; k += 4) {
+        const float4 y4 = *reinterpret_cast<const float4*>(&sY[q][k]);
+        Y[k] = y4.x;
+        Y[k + 1] = y4.y;
+        Y[k + 2] = y4.z;
+        Y[k + 3] = y4.w;
+        gY[k] = gY[k + 1] = gY[k + 2] = gY[k + 3] = 0.f;
+      }
       float gr = 0.f;
-      tp2_bwd(tab + row + c, st[q], x.rd.inv_h, X, scy[q], g, gX, gY, gr);
+      tp2_bwd(tab + row + c, st[q], x.rd.inv_h, X, Y, g, cg, gX, gY, gr);
       float* gxo = ev.GX2 + (size_t)j * 4 * MB_C + c;
 #pragma unroll
       for (int k = 0; k < 4; ++k) atomicAdd(gxo + k * MB_C, gX[k]);

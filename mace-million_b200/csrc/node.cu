@@ -3,40 +3,24 @@
 #include <float.h>
 
 #include "common.cuh"
+#include "gemm.cuh"
 #include "symcon_gen.cuh"
 
 namespace mb {
 
-// ------------------------------------------------------------------------------------------------ GEMM
-// Y[atom][yoff + m][:] (+)= alpha_atom * sum_s X[atom][xoff_s + m][:] @ B_s  (N = 128, K = nseg * 128).
-// Rows r = t * mult + m, atom = order ? order[t] : t.  Tile 64 rows x 128 columns, K step 32, 256 threads,
-// 4 x 8 outputs per thread.  (SIMT fp32 path.)
-struct GemmArgs {
-  const float* X;
-  int64_t ldx;
-  int xoff[4];
-  int nseg;
-  const float* B;
-  float* Y;
-  int64_t ldy;
-  int yoff;
-  int mult;
-  const int* order;
-  int n_atoms;
-  const float* rho;
-  int accumulate;
-};
-
+// ------------------------------------------------------------------------------------------------ GEMM (SIMT fp32)
+// Grouped problems (gemm.cuh).  Tile 64 rows x 128 columns, K step 32, 256 threads, 4 x 8 outputs per thread.
 constexpr int GBM = 64, GBN = 128, GBK = 32;
 
-__global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
+__global__ void __launch_bounds__(256) k_gemm(const __grid_constant__ GemmGroup grp) {
   __shared__ __align__(16) float As[GBK][GBM + 4];
   __shared__ __align__(16) float Bs[GBK][GBN];
+  const int pi = gemm_problem_of(grp, blockIdx.x);
+  const GemmProblem& g = grp.p[pi];
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   const int64_t nrows = (int64_t)g.n_atoms * g.mult;
-  const int64_t r0 = (int64_t)blockIdx.x * GBM;
-  // the A row this thread loads: r = r0 + tid / 4, k sub-block (tid % 4) * 8
+  const int64_t r0 = (int64_t)(blockIdx.x - grp.tile_start[pi]) * GBM;
   const int lr = tid >> 2, lk = (tid & 3) * 8;
   const int64_t rl = r0 + lr;
   const float* arow = nullptr;
@@ -114,31 +98,25 @@ __global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
   }
 }
 
+int gemm_group_launch_simt(const GemmGroup& grp0, cudaStream_t st) {
+  GemmGroup grp = grp0;
+  int tiles = 0;
+  for (int q = 0; q < grp.n; ++q) {
+    grp.tile_start[q] = tiles;
+    tiles += (int)(((int64_t)grp.p[q].n_atoms * grp.p[q].mult + GBM - 1) / GBM);
+  }
+  grp.tile_start[grp.n] = tiles;
+  if (tiles == 0) return 0;
+  k_gemm<<<tiles, 256, 0, st>>>(grp);
+  return check_launch("node_gemm");
+}
+
 int gemm_launch(const float* X, int64_t ldx, const int32_t* xoff, int nseg, const float* B, float* Y, int64_t ldy,
                 int yoff, int mult, const int32_t* order, int n_atoms, const float* rho, int accumulate,
                 cudaStream_t st) {
-  if (n_atoms <= 0) return 0;
-  if (!X || !B || !Y || !xoff || nseg < 1 || nseg > 4 || mult < 1 || (ldx % 4) || (ldy % 4)) {
-    set_error("node_gemm: bad arguments (nseg %d, mult %d)", nseg, mult);
-    return MB_E_ARG;
-  }
-  GemmArgs g;
-  g.X = X;
-  g.ldx = ldx;
-  for (int s = 0; s < 4; ++s) g.xoff[s] = s < nseg ? xoff[s] : 0;
-  g.nseg = nseg;
-  g.B = B;
-  g.Y = Y;
-  g.ldy = ldy;
-  g.yoff = yoff;
-  g.mult = mult;
-  g.order = order;
-  g.n_atoms = n_atoms;
-  g.rho = rho;
-  g.accumulate = accumulate;
-  const int64_t rows = (int64_t)n_atoms * mult;
-  k_gemm<<<(unsigned)((rows + GBM - 1) / GBM), 256, 0, st>>>(g);
-  return check_launch("node_gemm");
+  GemmBatch bt(false, nullptr, st);
+  int rc = bt.add(X, ldx, xoff, nseg, B, 0, Y, ldy, yoff, mult, order, n_atoms, rho, accumulate);
+  return rc ? rc : bt.launch();
 }
 
 // ------------------------------------------------------------------------------------------------ symmetric contraction

@@ -13,6 +13,7 @@
 #include <stdio.h>
 
 #include "common.cuh"
+#include "gemm.cuh"
 #include "tp_gen.cuh"
 
 namespace mb {
@@ -74,9 +75,6 @@ int check_launch(const char* what) {
   return 0;
 }
 
-int gemm_launch(const float* X, int64_t ldx, const int32_t* xoff, int nseg, const float* B, float* Y, int64_t ldy,
-                int yoff, int mult, const int32_t* order, int n_atoms, const float* rho, int accumulate,
-                cudaStream_t st);
 int symcon_fwd(const mb_model_t* m, int block, const float* x, float* A, const int32_t* spec, int n, cudaStream_t st);
 int symcon_bwd(const mb_model_t* m, int block, const float* x, const float* gA, float* gx, const int32_t* spec,
                const float* rho, float* grho, int n, cudaStream_t st);
@@ -101,6 +99,25 @@ int finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, doub
     if (_rc) return _rc;      \
   } while (0)
 
+// A weight matrix for the node GEMMs: SIMT fp32 row-major W, or its K-major tf32 hi / lo planes W_tc (`plane`
+// elements per plane) for the tcgen05 kernel; `off` selects one 128 x 128 (or multi-segment) matrix inside both.
+struct Wt {
+  const float* W;
+  const float* Wtc;
+  int64_t plane;
+};
+
+static int add(GemmBatch& gb, Wt w, size_t off, const float* X, int64_t ldx, const int32_t* xoff, int nseg, float* Y,
+               int64_t ldy, int yoff, int mult, const int32_t* order, int n, const float* rho, int acc) {
+  const float* B = gb.tc ? w.Wtc + off : w.W + off;
+  return gb.add(X, ldx, xoff, nseg, B, w.plane, Y, ldy, yoff, mult, order, n, rho, acc);
+}
+
+static bool use_tc(const mb_model_t* m) {
+  return m->use_tc && m->M0_tc && m->M0T_tc && m->Wp1_tc && m->Wp1T_tc && m->Wup2_tc && m->Wup2T_tc && m->Wsk1_tc &&
+         m->Wsk1T_tc && m->Wlin2_tc && m->Wlin2T_tc && m->Wp2_tc && m->Wp2T_tc;
+}
+
 static int check_pass_args(const mb_model_t* m, const mb_eval_t* ev, const char* who) {
   if (!m || !ev || ev->nl < 0 || ev->nt < ev->nl || ev->chunk <= 0 || m->S <= 0 || m->C != MB_C) {
     set_error("%s: bad model / eval arguments", who);
@@ -116,20 +133,17 @@ static int check_pass_args(const mb_model_t* m, const mb_eval_t* ev, const char*
 
 static const int kOffL[2] = {0, 1};      // component offset of the 0e / 1o blocks of h1-like [4][C] rows
 
-// x1 = msg1 M0[s] / (rho1 + 1) for one chunk, species segment by segment
+// x1 = msg1 M0[s] / (rho1 + 1) for one chunk: one problem per (l, species segment), one launch
 static int x1_gemms(const mb_model_t* m, const mb_eval_t* ev, int a, int ci, cudaStream_t st) {
   const int C = MB_C, S = m->S;
   const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
-  for (int l = 0; l < 4; ++l) {
-    const int off = l * l;
-    for (int s = 0; s < S; ++s) {
-      const int n = so[s + 1] - so[s];
-      if (n <= 0) continue;
-      RC(gemm_launch(ev->s_msg, 16 * C, &off, 1, m->M0 + ((size_t)s * 4 + l) * C * C, ev->s_x, 16 * C, off,
-                     2 * l + 1, ev->order + a + so[s], n, ev->s_rho, 0, st));
-    }
-  }
-  return 0;
+  GemmBatch gb(use_tc(m), ev->status, st);
+  static const int offs[4] = {0, 1, 4, 9};
+  for (int l = 0; l < 4; ++l)
+    for (int s = 0; s < S; ++s)
+      RC(add(gb, {m->M0, m->M0_tc, (int64_t)S * 4 * C * C}, ((size_t)s * 4 + l) * C * C, ev->s_msg, 16 * C, &offs[l],
+             1, ev->s_x, 16 * C, offs[l], 2 * l + 1, ev->order + a + so[s], so[s + 1] - so[s], ev->s_rho, 0));
+  return gb.launch();
 }
 
 }  // namespace mb
@@ -179,9 +193,11 @@ extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev, void* 
     TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
     RC(x1_gemms(m, ev, a, ci, st));
     TIMED(MB_K_SYMCON, symcon_fwd(m, 0, ev->s_x, ev->s_a, ev->spec + a, nC, st));
+    GemmBatch gb(use_tc(m), ev->status, st);
     for (int l = 0; l < 2; ++l)
-      RC(gemm_launch(ev->s_a, 4 * C, &kOffL[l], 1, m->Wp1 + (size_t)l * C * C, ev->H1 + (size_t)a * 4 * C, 4 * C,
-                     kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0, st));
+      RC(add(gb, {m->Wp1, m->Wp1_tc, 2 * C * C}, (size_t)l * C * C, ev->s_a, 4 * C, &kOffL[l], 1,
+             ev->H1 + (size_t)a * 4 * C, 4 * C, kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0));
+    RC(gb.launch());
   }
   return readout1(m, ev->H1, ev->eat, ev->nl, st);
 }
@@ -195,16 +211,18 @@ extern "C" int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* 
     set_error("x2_all: cudaMemsetAsync failed");
     return MB_E_CUDA;
   }
+  GemmBatch gb(use_tc(m), ev->status, st);
   for (int l = 0; l < 2; ++l)
-    RC(gemm_launch(ev->H1, 4 * C, &kOffL[l], 1, m->Wup2 + (size_t)l * C * C, ev->X2, 4 * C, kOffL[l], 2 * l + 1,
-                   nullptr, ev->nt, nullptr, 0, st));
-  return 0;
+    RC(add(gb, {m->Wup2, m->Wup2_tc, 2 * C * C}, (size_t)l * C * C, ev->H1, 4 * C, &kOffL[l], 1, ev->X2, 4 * C,
+           kOffL[l], 2 * l + 1, nullptr, ev->nt, nullptr, 0));
+  return gb.launch();
 }
 
 extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
   RC(check_pass_args(m, ev, "pass_b"));
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C, S = m->S;
+  const bool tc = use_tc(m);
   if (ev->P > 0 && cudaMemsetAsync(ev->PF, 0, (size_t)ev->P * 3 * sizeof(float), st) != cudaSuccess) {
     set_error("pass_b: cudaMemsetAsync(PF) failed");
     return MB_E_CUDA;
@@ -213,70 +231,85 @@ extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* 
   for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
     const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
-    // sc = skip_tp(h1_0e, species)
-    for (int s = 0; s < S; ++s) {
-      const int n = so[s + 1] - so[s];
-      if (n > 0)
-        RC(gemm_launch(ev->H1 + (size_t)a * 4 * C, 4 * C, &zero, 1, m->Wsk1 + (size_t)s * C * C, ev->s_sc, C, 0, 1,
-                       ev->order + a + so[s], n, nullptr, 0, st));
-    }
     TIMED(MB_K_EDGE_L2_FWD, mace_b200_edge_l2_fwd(m, ev, a, b, st));
-    // x2 = linear(msg2) / (rho2 + 1), per output l over its mid copies
-    for (int l = 0; l < 4; ++l) {
-      int xoff[4];
-      for (int j = 0; j < TP2_GROUP_N[l]; ++j) xoff[j] = TP2_MID_OFF[TP2_GROUP_W0[l] + j];
-      RC(gemm_launch(ev->s_msg, TP2_NO * C, xoff, TP2_GROUP_N[l], m->Wlin2 + (size_t)TP2_GROUP_W0[l] * C * C,
-                     ev->s_x, 16 * C, l * l, 2 * l + 1, nullptr, nC, ev->s_rho, 0, st));
+    {
+      // sc = skip_tp(h1_0e, species) and x2 = linear(msg2) / (rho2 + 1) per output l over its mid copies
+      GemmBatch gb(tc, ev->status, st);
+      for (int s = 0; s < S; ++s)
+        RC(add(gb, {m->Wsk1, m->Wsk1_tc, (int64_t)S * C * C}, (size_t)s * C * C, ev->H1 + (size_t)a * 4 * C, 4 * C,
+               &zero, 1, ev->s_sc, C, 0, 1, ev->order + a + so[s], so[s + 1] - so[s], nullptr, 0));
+      for (int l = 0; l < 4; ++l) {
+        int xoff[4];
+        for (int j = 0; j < TP2_GROUP_N[l]; ++j) xoff[j] = TP2_MID_OFF[TP2_GROUP_W0[l] + j];
+        RC(add(gb, {m->Wlin2, m->Wlin2_tc, (int64_t)TP2_NW * C * C}, (size_t)TP2_GROUP_W0[l] * C * C, ev->s_msg,
+               TP2_NO * C, xoff, TP2_GROUP_N[l], ev->s_x, 16 * C, l * l, 2 * l + 1, nullptr, nC, ev->s_rho, 0));
+      }
+      RC(gb.launch());
     }
     TIMED(MB_K_SYMCON, symcon_fwd(m, 1, ev->s_x, ev->s_a, ev->spec + a, nC, st));
-    RC(gemm_launch(ev->s_a, C, &zero, 1, m->Wp2, ev->s_sc, C, 0, 1, nullptr, nC, nullptr, 1, st));   // h2 in s_sc
+    {
+      GemmBatch gb(tc, ev->status, st);   // h2 = sc + A2 Wp2 (in s_sc)
+      RC(add(gb, {m->Wp2, m->Wp2_tc, C * C}, 0, ev->s_a, C, &zero, 1, ev->s_sc, C, 0, 1, nullptr, nC, nullptr, 1));
+      RC(gb.launch());
+    }
     RC(readout2(m, ev->s_sc, ev->eat + a, ev->s_gh, nC, st));
-    RC(gemm_launch(ev->s_gh, C, &zero, 1, m->Wp2T, ev->s_ga, C, 0, 1, nullptr, nC, nullptr, 0, st));
-    for (int s = 0; s < S; ++s) {
-      const int n = so[s + 1] - so[s];
-      if (n > 0)
-        RC(gemm_launch(ev->s_gh, C, &zero, 1, m->Wsk1T + (size_t)s * C * C, ev->G1 + (size_t)a * 4 * C, 4 * C, 0, 1,
-                       ev->order + a + so[s], n, nullptr, 1, st));
+    {
+      GemmBatch gb(tc, ev->status, st);   // gA2 = g_h2 Wp2^T;  G1[a:b]_0e += g_h2 Wsk1[s]^T
+      RC(add(gb, {m->Wp2T, m->Wp2T_tc, C * C}, 0, ev->s_gh, C, &zero, 1, ev->s_ga, C, 0, 1, nullptr, nC, nullptr, 0));
+      for (int s = 0; s < S; ++s)
+        RC(add(gb, {m->Wsk1T, m->Wsk1T_tc, (int64_t)S * C * C}, (size_t)s * C * C, ev->s_gh, C, &zero, 1,
+               ev->G1 + (size_t)a * 4 * C, 4 * C, 0, 1, ev->order + a + so[s], so[s + 1] - so[s], nullptr, 1));
+      RC(gb.launch());
     }
     TIMED(MB_K_SYMCON, symcon_bwd(m, 1, ev->s_x, ev->s_ga, ev->s_gx, ev->spec + a, ev->s_rho, ev->s_grho, nC, st));
-    for (int l = 0; l < 4; ++l) {
-      const int off = l * l;
-      for (int j = 0; j < TP2_GROUP_N[l]; ++j) {
-        const int w = TP2_GROUP_W0[l] + j;
-        RC(gemm_launch(ev->s_gx, 16 * C, &off, 1, m->Wlin2T + (size_t)w * C * C, ev->s_msg, TP2_NO * C,
-                       TP2_MID_OFF[w], 2 * l + 1, nullptr, nC, ev->s_rho, 0, st));
-      }
+    {
+      GemmBatch gb(tc, ev->status, st);   // g_msg2 = g_x2 lin2^T / (rho2 + 1), one problem per mid entry
+      static const int offs[4] = {0, 1, 4, 9};
+      for (int l = 0; l < 4; ++l)
+        for (int j = 0; j < TP2_GROUP_N[l]; ++j) {
+          const int w = TP2_GROUP_W0[l] + j;
+          RC(add(gb, {m->Wlin2T, m->Wlin2T_tc, (int64_t)TP2_NW * C * C}, (size_t)w * C * C, ev->s_gx, 16 * C,
+                 &offs[l], 1, ev->s_msg, TP2_NO * C, TP2_MID_OFF[w], 2 * l + 1, nullptr, nC, ev->s_rho, 0));
+        }
+      RC(gb.launch());
     }
     TIMED(MB_K_EDGE_L2_BWD, mace_b200_edge_l2_bwd(m, ev, a, b, st));
   }
+  GemmBatch gb(tc, ev->status, st);
   for (int l = 0; l < 2; ++l)
-    RC(gemm_launch(ev->GX2, 4 * C, &kOffL[l], 1, m->Wup2T + (size_t)l * C * C, ev->G1, 4 * C, kOffL[l], 2 * l + 1,
-                   nullptr, ev->nt, nullptr, 1, st));
-  return 0;
+    RC(add(gb, {m->Wup2T, m->Wup2T_tc, 2 * C * C}, (size_t)l * C * C, ev->GX2, 4 * C, &kOffL[l], 1, ev->G1, 4 * C,
+           kOffL[l], 2 * l + 1, nullptr, ev->nt, nullptr, 1));
+  return gb.launch();
 }
 
 extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
   RC(check_pass_args(m, ev, "pass_c"));
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C, S = m->S;
+  const bool tc = use_tc(m);
+  static const int offs[4] = {0, 1, 4, 9};
   for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
     const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
     TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
     RC(x1_gemms(m, ev, a, ci, st));
     RC(gh1(m, ev->G1 + (size_t)a * 4 * C, ev->s_a, nC, st));
-    for (int l = 0; l < 2; ++l)
-      RC(gemm_launch(ev->s_a, 4 * C, &kOffL[l], 1, m->Wp1T + (size_t)l * C * C, ev->s_ga, 4 * C, kOffL[l],
-                     2 * l + 1, nullptr, nC, nullptr, 0, st));
+    {
+      GemmBatch gb(tc, ev->status, st);   // gA1 = g_h1 Wp1^T
+      for (int l = 0; l < 2; ++l)
+        RC(add(gb, {m->Wp1T, m->Wp1T_tc, 2 * C * C}, (size_t)l * C * C, ev->s_a, 4 * C, &kOffL[l], 1, ev->s_ga,
+               4 * C, kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0));
+      RC(gb.launch());
+    }
     TIMED(MB_K_SYMCON, symcon_bwd(m, 0, ev->s_x, ev->s_ga, ev->s_gx, ev->spec + a, ev->s_rho, ev->s_grho, nC, st));
-    for (int l = 0; l < 4; ++l) {
-      const int off = l * l;
-      for (int s = 0; s < S; ++s) {
-        const int n = so[s + 1] - so[s];
-        if (n <= 0) continue;
-        RC(gemm_launch(ev->s_gx, 16 * C, &off, 1, m->M0T + ((size_t)s * 4 + l) * C * C, ev->s_msg, 16 * C, off,
-                       2 * l + 1, ev->order + a + so[s], n, ev->s_rho, 0, st));
-      }
+    {
+      GemmBatch gb(tc, ev->status, st);   // g_msg1 = g_x1 M0[s]^T / (rho1 + 1)
+      for (int l = 0; l < 4; ++l)
+        for (int s = 0; s < S; ++s)
+          RC(add(gb, {m->M0T, m->M0T_tc, (int64_t)S * 4 * C * C}, ((size_t)s * 4 + l) * C * C, ev->s_gx, 16 * C,
+                 &offs[l], 1, ev->s_msg, 16 * C, offs[l], 2 * l + 1, ev->order + a + so[s], so[s + 1] - so[s],
+                 ev->s_rho, 0));
+      RC(gb.launch());
     }
     TIMED(MB_K_EDGE_L1_BWD, mace_b200_edge_l1_bwd(m, ev, a, b, st));
   }

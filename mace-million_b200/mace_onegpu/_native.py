@@ -22,7 +22,10 @@ class MBModel(ctypes.Structure):
                 ("tab1", c_vp), ("tab2", c_vp), ("wd1", c_vp), ("wd2", c_vp),
                 ("M0", c_vp), ("M0T", c_vp), ("Wp1", c_vp), ("Wp1T", c_vp), ("wr0", c_vp), ("sc1", c_vp),
                 ("Wup2", c_vp), ("Wup2T", c_vp), ("Wsk1", c_vp), ("Wsk1T", c_vp), ("Wlin2", c_vp), ("Wlin2T", c_vp),
-                ("sc2", c_vp), ("Wp2", c_vp), ("Wp2T", c_vp), ("W1r", c_vp), ("w2r", c_vp), ("e0", c_vp)]
+                ("sc2", c_vp), ("Wp2", c_vp), ("Wp2T", c_vp), ("W1r", c_vp), ("w2r", c_vp), ("e0", c_vp),
+                ("M0_tc", c_vp), ("M0T_tc", c_vp), ("Wp1_tc", c_vp), ("Wp1T_tc", c_vp), ("Wup2_tc", c_vp),
+                ("Wup2T_tc", c_vp), ("Wsk1_tc", c_vp), ("Wsk1T_tc", c_vp), ("Wlin2_tc", c_vp), ("Wlin2T_tc", c_vp),
+                ("Wp2_tc", c_vp), ("Wp2T_tc", c_vp), ("use_tc", c_i32)]
 
 
 class MBEval(ctypes.Structure):
@@ -56,6 +59,8 @@ _SIGS = {
                                       c_i32, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mace_b200_node_gemm": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp,
                                     c_i32, c_vp]),
+    "mace_b200_node_gemm_tc": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32,
+                                       c_vp, c_i32, c_vp, c_vp]),
     "mace_b200_symcon_fwd": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i32, c_vp]),
     "mace_b200_symcon_bwd": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_vp]),
     "mace_b200_pass_a": (c_i32, [c_vp, c_vp, c_vp]),

@@ -31,6 +31,23 @@ def _f32(t, device):
     return torch.as_tensor(t, dtype=torch.float64).to(dtype=torch.float32, device=device).contiguous()
 
 
+def tf32_rna(x: np.ndarray) -> np.ndarray:
+    """Round fp32 values to tf32 (10 mantissa bits), to nearest with ties away from zero (PTX cvt.rna.tf32.f32)."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = ((b & 0x7FFFFFFF) + np.uint32(0x1000)) & np.uint32(0x7FFFE000)
+    r = r | (b & np.uint32(0x80000000))
+    finite = (b & 0x7F800000) != 0x7F800000
+    return np.where(finite, r, b).view(np.float32)
+
+
+def tc_split(B: np.ndarray) -> np.ndarray:
+    """K-major 3xTF32 planes of matrices B [..., K, N] used as GEMM B operands: [2][..., N, K] (hi, lo)."""
+    bt = np.ascontiguousarray(np.swapaxes(np.asarray(B, dtype=np.float64), -1, -2)).astype(np.float32)
+    hi = tf32_rna(bt)
+    lo = tf32_rna(bt - hi)
+    return np.ascontiguousarray(np.stack([hi, lo]))
+
+
 def fold_weights(model: Mdl.MACEModel, cols) -> dict:
     """All folded fp64 arrays (CPU numpy) for the species columns `cols` (model one-hot columns present)."""
     a = model.arch
@@ -87,8 +104,11 @@ def fold_weights(model: Mdl.MACEModel, cols) -> dict:
 class FoldedModel:
     """Device-resident folded model for one species subset (the ctypes mb_model_t points into its tensors)."""
 
-    def __init__(self, model: Mdl.MACEModel, cols, spline_grid: int = 512, r_lo: float = 0.5, device="cuda"):
+    def __init__(self, model: Mdl.MACEModel, cols, spline_grid: int = 512, r_lo: float = 0.5, device="cuda",
+                 use_tc: bool | None = None):
         L = N.lib()
+        if use_tc is None:
+            use_tc = os.environ.get("MACE_B200_TC", "1") != "0"
         self.cols = [int(c) for c in cols]
         self.device = torch.device(device)
         a = model.arch
@@ -130,6 +150,11 @@ class FoldedModel:
         t["W1r"] = _f32(f["W1r"], dev)
         t["w2r"] = _f32(f["w2r"], dev)
         t["e0"] = torch.as_tensor(f["e0"], dtype=torch.float64, device=dev).contiguous()
+        for name, key, transpose in (("M0", "M0", False), ("Wp1", "Wp1", False), ("Wup2", "Wup2", False),
+                                     ("Wsk1", "Wsk1", False), ("Wlin2", "Wlin2", False), ("Wp2", "Wp2", False)):
+            W = f[key]
+            t[name + "_tc"] = torch.as_tensor(tc_split(W), device=dev).contiguous()
+            t[name + "T_tc"] = torch.as_tensor(tc_split(np.swapaxes(W, -1, -2)), device=dev).contiguous()
         # spline tables built on the GPU in fp64 (tab1 carries X1 of the sender species)
         self.TV, self.TG = {}, {}
         for i, key, D, csk in ((0, "tab1", 4 * C, "col_scale1"), (1, "tab2", 10 * C, None)):
@@ -149,8 +174,9 @@ class FoldedModel:
         self.t = t
         h = (self.r_max - self.r_lo) / (self.M - 1)
         self.struct = N.MBModel(C=C, S=S, M=self.M, r_lo=self.r_lo, inv_h=1.0 / h, r_max=self.r_max,
-                                p_cut=float(a.num_poly_cutoff), scale=self.scale,
+                                p_cut=float(a.num_poly_cutoff), scale=self.scale, use_tc=1 if use_tc else 0,
                                 **{k: N.ptr(v) for k, v in t.items() if not k.startswith("_")})
+        self.use_tc = bool(use_tc)
 
 
 class Plan:
@@ -192,11 +218,12 @@ class Plan:
 class ThreePassEngine:
     """The three-pass evaluation on one GPU for a fixed model and species set."""
 
-    def __init__(self, model: Mdl.MACEModel, cols, chunk: int = 16384, spline_grid: int = 512, device="cuda"):
+    def __init__(self, model: Mdl.MACEModel, cols, chunk: int = 16384, spline_grid: int = 512, device="cuda",
+                 use_tc: bool | None = None):
         self.device = torch.device(device)
         self.model = model
         self.chunk = int(chunk)
-        self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device)
+        self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device, use_tc=use_tc)
         Zn = len(model.arch.atomic_numbers)
         col2s = torch.full((Zn,), -1, dtype=torch.int64)
         col2s[torch.as_tensor(self.fm.cols)] = torch.arange(len(self.fm.cols))
@@ -238,7 +265,8 @@ class ThreePassEngine:
         if s:
             names = [n for bit, n in ((1, "sender index out of range"), (2, "species out of range"),
                                       (4, "bad CSR row pointer"), (8, "non-finite or zero edge vector"),
-                                      (16, "pair_i does not match its CSR row")) if s & bit]
+                                      (16, "pair_i does not match its CSR row"),
+                                      (32, "tensor-core GEMM barrier wait expired")) if s & bit]
             raise RuntimeError(f"mace_b200 {what}: input error reported by the kernels: {', '.join(names)}")
 
     # ------------------------------------------------------------------------------------------------ evaluation

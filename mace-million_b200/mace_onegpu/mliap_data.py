@@ -16,7 +16,8 @@ import torch
 
 
 class MLIAPData:
-    def __init__(self, pair_i, pair_j, rij, elems, nlocal: int, owner=None, host_outputs: bool = False):
+    def __init__(self, pair_i, pair_j, rij, elems, nlocal: int, owner=None, host_outputs: bool = False,
+                 exchange=None):
         self.pair_i = pair_i
         self.pair_j = pair_j
         self.rij = rij
@@ -33,6 +34,7 @@ class MLIAPData:
         self._pf_host = torch.empty((self.npairs, 3), dtype=torch.float64, pin_memory=pin) if host_outputs else None
         self.owner = None if owner is None else torch.as_tensor(owner).long()
         self._owner_dev = {}
+        self.exchange = exchange          # distributed halo exchange (forward(H) / reverse(G) in place), e.g. domain.py
 
     def _own(self, device):
         o = self._owner_dev.get(device)
@@ -43,13 +45,17 @@ class MLIAPData:
 
     def forward_exchange(self, src, dst, D):
         dst.copy_(src)
-        if self.owner is not None and self.ntotal > self.nlocal:
+        if self.exchange is not None:
+            self.exchange.forward(dst)
+        elif self.owner is not None and self.ntotal > self.nlocal:
             own = self._own(src.device)
             dst[self.nlocal:] = src[own[self.nlocal:]]
 
     def reverse_exchange(self, src, dst, D):
         dst.copy_(src)
-        if self.owner is not None and self.ntotal > self.nlocal:
+        if self.exchange is not None:
+            self.exchange.reverse(dst)
+        elif self.owner is not None and self.ntotal > self.nlocal:
             own = self._own(src.device)
             dst.index_add_(0, own[self.nlocal:], src[self.nlocal:])
             dst[self.nlocal:] = 0

@@ -265,9 +265,12 @@ class MaceRef:
         return eat.detach(), gv.detach()
 
     # ------------------------------------------------------------------------------------------ three pass
-    def three_pass(self, pi, pj, rij, elems, nl, chunk, owner=None, return_state=False):
+    def three_pass(self, pi, pj, rij, elems, nl, chunk, owner=None, return_state=False, forward_exchange=None,
+                   reverse_exchange=None):
         """The receiver-chunked three-pass evaluation with ML-IAP semantics; returns (eatoms [nl], PF [P, 3]) and,
-        with return_state, also H1 [nt, C, 4] after the forward exchange and G1r [nl, C, 4] after the reverse one."""
+        with return_state, also H1 [nt, C, 4] after the forward exchange and G1r [nl, C, 4] after the reverse one.
+        forward_exchange / reverse_exchange (rows [nt, C*4], in place) replace the owner map, e.g. with the
+        distributed halo exchange of a domain decomposition."""
         pi, pj = torch.as_tensor(pi).long(), torch.as_tensor(pj).long()
         elems = torch.as_tensor(elems).long()
         nt = elems.numel()
@@ -286,7 +289,10 @@ class MaceRef:
             for a, b in bounds:
                 e0, e1 = int(rp[a]), int(rp[b])
                 H1[a:b] = self._chunk_l1(a, b, e0, e1, pi_s, pj_s, rij_s, elems, None)
-        H1[nl:] = H1[owner[nl:]]                                                          # forward exchange
+        if forward_exchange is not None:
+            forward_exchange(H1.view(nt, -1))
+        else:
+            H1[nl:] = H1[owner[nl:]]                                                      # forward exchange
         # pass B
         G1 = torch.zeros_like(H1)
         for a, b in bounds:
@@ -304,8 +310,13 @@ class MaceRef:
             PF[order[e0:e1]] += gv
             G1.index_add_(0, nodes, gh)
             eat[a:b] += self.scale * R2.detach()
-        G1r = G1[:nl].clone()
-        G1r.index_add_(0, owner[nl:], G1[nl:])                                            # reverse exchange
+        if reverse_exchange is not None:
+            G = G1.clone()
+            reverse_exchange(G.view(nt, -1))
+            G1r = G[:nl].clone()
+        else:
+            G1r = G1[:nl].clone()
+            G1r.index_add_(0, owner[nl:], G1[nl:])                                        # reverse exchange
         # pass C
         for a, b in bounds:
             e0, e1 = int(rp[a]), int(rp[b])

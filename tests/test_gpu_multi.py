@@ -1,0 +1,100 @@
+"""Multi-GPU parity: the three-pass evaluation split over 2 GPUs by spatial domains (explicit ghosts, H1 forward /
+G1 reverse halo exchange over NCCL) reproduces the single-process fp64 oracle.  Needs >= 2 GPUs (skipped otherwise);
+ranks run as child processes; NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout."""
+import dataclasses
+import os
+import queue
+import socket
+import time
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from mace_onegpu import domain as D
+from mace_onegpu import model as M
+from mace_onegpu import neighbors as NB
+from mace_onegpu import structures as S
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, grid, out_q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from mace_onegpu.engine import ThreePassEngine
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        mdl = M.default_model(0)
+        pos, Z, box = S.water_box(8, 4, 4, seed=2)
+        cols = S.species_columns(Z, mdl.arch.atomic_numbers)
+        dec = D.Decomposition(pos, box, grid, mdl.arch.r_max + 2.0)
+        p, gid, nl = dec.rank_atoms(rank)
+        pi, pj, rij = NB.neighbor_list_open(p, nl, mdl.arch.r_max, device=dev)
+        eng = ThreePassEngine(mdl, sorted(set(cols.tolist())), chunk=100, device=dev)
+        hx = D.HaloExchange(dec, rank, dev)
+        plan = eng.plan(pi, pj, rij, torch.as_tensor(cols[gid]), nl, len(gid))
+        eat, pf = eng.evaluate(plan, hx.forward, hx.reverse)
+        torch.cuda.synchronize()
+        n = len(Z)
+        E = torch.zeros(n, dtype=torch.float64, device=dev)
+        E[torch.as_tensor(gid[:nl], device=dev)] = eat
+        F = torch.zeros(n, 3, dtype=torch.float64, device=dev)
+        gi = torch.as_tensor(gid, device=dev)
+        F.index_add_(0, gi[pi.long()], -pf)
+        F.index_add_(0, gi[pj.long()], pf)
+        dist.all_reduce(E)
+        dist.all_reduce(F)
+        if rank == 0:
+            out_q.put((E.cpu().numpy(), F.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_domain_decomposition_matches_oracle():
+    from oracle import mace_ref
+
+    grid, world = (2, 1, 1), 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, grid, q)) for r in range(world)]
+    for p_ in procs:
+        p_.start()
+    t0 = time.time()
+    while True:
+        try:
+            E, F = q.get(timeout=2)
+            break
+        except queue.Empty:
+            dead = [p_.exitcode for p_ in procs if p_.exitcode not in (None, 0)]
+            assert not dead and time.time() - t0 < 600, f"rank failed: exit codes {dead}"
+    for p_ in procs:
+        p_.join(timeout=120)
+        assert p_.exitcode == 0
+    mdl = M.default_model(0)
+    pos, Z, box = S.water_box(8, 4, 4, seed=2)
+    cols = S.species_columns(Z, mdl.arch.atomic_numbers)
+    pi, pj, rij = NB.neighbor_list(pos, box, mdl.arch.r_max)
+    ref = mace_ref.MaceRef(mdl.params(), dataclasses.asdict(mdl.arch), spline_knots=512)
+    e0, pf0 = ref.three_pass(pi, pj, rij, cols, len(Z), 128)
+    F0 = mace_ref.atom_forces(pi, pj, pf0, len(Z)).numpy()
+    assert np.abs(E - e0.numpy()).max() < 1e-5
+    assert np.abs(F - F0).max() < 1e-3

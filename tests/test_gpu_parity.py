@@ -43,8 +43,8 @@ def oracle(mdl, water):
     return dict(ref=ref, eat=eat, pf=pf, H1=H1, G1r=G1r)
 
 
-def _engine(mdl, cols, chunk):
-    return E.ThreePassEngine(mdl, sorted(set(int(c) for c in cols)), chunk=chunk, device="cuda")
+def _engine(mdl, cols, chunk, use_tc=None):
+    return E.ThreePassEngine(mdl, sorted(set(int(c) for c in cols)), chunk=chunk, device="cuda", use_tc=use_tc)
 
 
 def test_tables_match_oracle(mdl, water, oracle):
@@ -109,8 +109,9 @@ def test_g1_matches_oracle(mdl, water, oracle):
     assert err <= 2e-5 * want.abs().max().item(), err
 
 
-def test_energy_and_forces_match_oracle(mdl, water, oracle):
-    eng = _engine(mdl, water["cols"], 64)
+@pytest.mark.parametrize("use_tc", [True, False], ids=["tcgen05", "simt"])
+def test_energy_and_forces_match_oracle(mdl, water, oracle, use_tc):
+    eng = _engine(mdl, water["cols"], 64, use_tc=use_tc)
     eat, pf, _ = _run(eng, water)
     de, dpf, dF = _compare(eat, pf, oracle, water)
     assert de < E_TOL and dF < F_TOL and dpf < F_TOL
