@@ -116,6 +116,11 @@ typedef struct {
   float* s_rho;                /* [chunk] */
   float* s_grho;               /* [chunk] */
   uint32_t* status;            /* device status word */
+  /* optional cache of pass A's layer-1 intermediates for pass C (null = recompute them, the reference's
+   * low-memory schedule): x1 = linear_1(msg1) / (rho1 + 1) [nl][16][C] and rho1 [nl].  Pass C reads them
+   * instead of re-running edge_l1_fwd and the x1 GEMMs; the values are bitwise the same (deterministic kernels). */
+  float* x1_cache;
+  float* rho1_cache;
 } mb_eval_t;
 
 /* ---------------------------------------------------------------- library info */

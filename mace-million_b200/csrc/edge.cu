@@ -93,165 +93,186 @@ __device__ __forceinline__ float block_sum128(float v, float* red4) {
   return red4[0] + red4[1] + red4[2] + red4[3];
 }
 
-// ------------------------------------------------------------------------------------------------ layer 1 forward
-// s_msg[i][lm][c] = sum_e T1(r_e; pair_e)[l][c] * Y_e[lm];  s_rho[i] = sum_e tanh(d_e^2)
-template <int EB>
-__global__ void __launch_bounds__(128) k_edge_l1_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
-  __shared__ float sY[EB][16];
-  __shared__ int srow[EB];
-  __shared__ float st[EB];
-  __shared__ float red4[4];
+// ------------------------------------------------------------------------------------------------ layer 1
+// Layer-1 edge kernels (pass A / C forward: s_msg[i][lm][c] = sum_e T1(r_e; pair_e)[l][c] Y_e[lm], s_rho[i];
+// pass C backward: PF[e] += dL/dv_e from g = dL/dmsg1 in s_msg and s_grho): one warp per receiver, lane = channels lane + 32 j (j = 0..3, so every load and store
+// of the warp is one contiguous 512-byte row); the warp's lanes run the per-edge prologue for batches of 32 edges
+// into warp-private shared memory; 4 receivers per CTA, no CTA-wide barrier.  The backward forms per lane
+// Q[lm] = sum_{its 4 channels} g[lm][c] T[l][c] and contracts it with the SH Jacobian once per 4 channels.
+constexpr int L1_WARPS = 4;
+
+__global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_fwd(const mb_model_t m, const mb_eval_t ev, int a, int b) {
+  __shared__ __align__(16) float sY[L1_WARPS][32][16];
+  __shared__ int srow[L1_WARPS][32];
+  __shared__ float st[L1_WARPS][32];
   const EdgeCtx x = make_ctx(m, ev);
-  const int il = blockIdx.x, i = a + il, c = threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int il = blockIdx.x * L1_WARPS + warp, i = a + il;
+  if (i >= b) return;
   int64_t e0, e1;
   if (!row_range(ev, i, e0, e1)) return;
   const float4* tab = reinterpret_cast<const float4*>(m.tab1);
-  float acc[16];
+  float acc[16][4];
 #pragma unroll
-  for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+  for (int q = 0; q < 16; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
   float rho = 0.f;
-  for (int64_t base = e0; base < e1; base += EB) {
-    const int n = (int)min((int64_t)EB, e1 - base);
-    __syncthreads();
-    if (c < n) {
+  for (int64_t base = e0; base < e1; base += 32) {
+    const int n = (int)min((int64_t)32, e1 - base);
+    __syncwarp();
+    if (lane < n) {
       float3 v;
       float r;
       int j, pair;
       int row = -1;
-      if (edge_geom(ev, x, base + c, i, v, r, j, pair)) {
+      if (edge_geom(ev, x, base + lane, i, v, r, j, pair)) {
         int k;
         float t;
         spline_coords(r, x.rd, k, t);
         row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
-        st[c] = t;
+        st[warp][lane] = t;
         const float ir = 1.f / r;
         float Y[16];
         sh16<float>(v.x * ir, v.y * ir, v.z * ir, Y);
 #pragma unroll
-        for (int q = 0; q < 16; ++q) sY[c][q] = Y[q];
+        for (int q = 0; q < 16; ++q) sY[warp][lane][q] = Y[q];
         float ed, ded;
         edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
         rho += ed;
       }
-      srow[c] = row;
+      srow[warp][lane] = row;
     }
-    __syncthreads();
+    __syncwarp();
     for (int q = 0; q < n; ++q) {
-      const int row = srow[q];
+      const int row = srow[warp][q];
       if (row < 0) continue;
-      const float t = st[q];
-      const float4* rw = tab + row + c;
-      const float T0 = cubic(__ldg(rw), t);
-      const float T1 = cubic(__ldg(rw + MB_C), t);
-      const float T2 = cubic(__ldg(rw + 2 * MB_C), t);
-      const float T3 = cubic(__ldg(rw + 3 * MB_C), t);
-      const float* Y = sY[q];
-      acc[0] = fmaf(T0, Y[0], acc[0]);
+      const float t = st[warp][q];
+      const float4* rw = tab + row + lane;
+      float Y[16];
 #pragma unroll
-      for (int mm = 1; mm < 4; ++mm) acc[mm] = fmaf(T1, Y[mm], acc[mm]);
+      for (int k = 0; k < 16; k += 4) {
+        const float4 y4 = *reinterpret_cast<const float4*>(&sY[warp][q][k]);
+        Y[k] = y4.x; Y[k + 1] = y4.y; Y[k + 2] = y4.z; Y[k + 3] = y4.w;
+      }
 #pragma unroll
-      for (int mm = 4; mm < 9; ++mm) acc[mm] = fmaf(T2, Y[mm], acc[mm]);
+      for (int l = 0; l < 4; ++l) {
+        float T[4];
 #pragma unroll
-      for (int mm = 9; mm < 16; ++mm) acc[mm] = fmaf(T3, Y[mm], acc[mm]);
+        for (int jj = 0; jj < 4; ++jj) T[jj] = cubic(__ldg(rw + l * MB_C + 32 * jj), t);
+#pragma unroll
+        for (int mm = l * l; mm < (l + 1) * (l + 1); ++mm)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) acc[mm][jj] = fmaf(T[jj], Y[mm], acc[mm][jj]);
+      }
     }
   }
-  float* out = ev.s_msg + (size_t)il * 16 * MB_C + c;
+  float* out = ev.s_msg + (size_t)il * 16 * MB_C + lane;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) out[q * MB_C] = acc[q];
-  rho = block_sum128(rho, red4);
-  if (c == 0) ev.s_rho[il] = rho;
+  for (int q = 0; q < 16; ++q)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) out[q * MB_C + 32 * jj] = acc[q][jj];
+  rho = warp_sum(rho);
+  if (lane == 0) ev.s_rho[il] = rho;
 }
 
-// ------------------------------------------------------------------------------------------------ layer 1 backward
-// Pass C: given g = dL/dmsg1 (s_msg, [i][16][C]) and s_grho, PF[e] += dL/dv_e.
-template <int EB>
-__global__ void __launch_bounds__(128) k_edge_l1_bwd(const mb_model_t m, const mb_eval_t ev, int a) {
-  __shared__ float sY[EB][16];
-  __shared__ float sJ[EB][48];
-  __shared__ float su[EB][3];
-  __shared__ float sgd[EB];
-  __shared__ int srow[EB];
-  __shared__ float st[EB];
-  __shared__ float sred[EB][4][3];
+__global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_bwd(const mb_model_t m, const mb_eval_t ev, int a, int b) {
+  __shared__ __align__(16) float sY[L1_WARPS][32][16];
+  __shared__ __align__(16) float sJ[L1_WARPS][32][48];
+  __shared__ float su[L1_WARPS][32][4];
+  __shared__ int srow[L1_WARPS][32];
+  __shared__ float st[L1_WARPS][32];
   const EdgeCtx x = make_ctx(m, ev);
-  const int il = blockIdx.x, i = a + il, c = threadIdx.x, warp = c >> 5, lane = c & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int il = blockIdx.x * L1_WARPS + warp, i = a + il;
+  if (i >= b) return;
   int64_t e0, e1;
   if (!row_range(ev, i, e0, e1)) return;
   const float4* tab = reinterpret_cast<const float4*>(m.tab1);
-  float g[16];
-  const float* gin = ev.s_msg + (size_t)il * 16 * MB_C + c;
+  float g[16][4];
+  const float* gin = ev.s_msg + (size_t)il * 16 * MB_C + lane;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) g[q] = gin[q * MB_C];
+  for (int q = 0; q < 16; ++q)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) g[q][jj] = gin[q * MB_C + 32 * jj];
   const float grho = ev.s_grho[il];
-  for (int64_t base = e0; base < e1; base += EB) {
-    const int n = (int)min((int64_t)EB, e1 - base);
-    __syncthreads();
-    if (c < n) {
+  for (int64_t base = e0; base < e1; base += 32) {
+    const int n = (int)min((int64_t)32, e1 - base);
+    __syncwarp();
+    if (lane < n) {
       float3 v;
       float r;
       int j, pair;
       int row = -1;
-      if (edge_geom(ev, x, base + c, i, v, r, j, pair)) {
+      if (edge_geom(ev, x, base + lane, i, v, r, j, pair)) {
         int k;
         float t;
         spline_coords(r, x.rd, k, t);
         row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
-        st[c] = t;
+        st[warp][lane] = t;
         const float ir = 1.f / r;
         float3 u = make_float3(v.x * ir, v.y * ir, v.z * ir);
-        sh_jacobian(u, r, sY[c], sJ[c]);
-        su[c][0] = u.x;
-        su[c][1] = u.y;
-        su[c][2] = u.z;
+        sh_jacobian(u, r, sY[warp][lane], sJ[warp][lane]);
         float ed, ded;
         edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
-        sgd[c] = grho * ded;
+        su[warp][lane][0] = u.x;
+        su[warp][lane][1] = u.y;
+        su[warp][lane][2] = u.z;
+        su[warp][lane][3] = grho * ded;
       }
-      srow[c] = row;
+      srow[warp][lane] = row;
     }
-    __syncthreads();
+    __syncwarp();
     for (int q = 0; q < n; ++q) {
-      const int row = srow[q];
+      const int row = srow[warp][q];
       if (row < 0) continue;
-      const float t = st[q];
-      const float4* rw = tab + row + c;
-      const float* Y = sY[q];
-      const float* J = sJ[q];
-      float gr = 0.f, gvx = 0.f, gvy = 0.f, gvz = 0.f;
+      const float t = st[warp][q];
+      const float4* rw = tab + row + lane;
+      float Y[16];
+#pragma unroll
+      for (int k = 0; k < 16; k += 4) {
+        const float4 y4 = *reinterpret_cast<const float4*>(&sY[warp][q][k]);
+        Y[k] = y4.x; Y[k + 1] = y4.y; Y[k + 2] = y4.z; Y[k + 3] = y4.w;
+      }
+      float Q[16];
+      float gr = 0.f;
 #pragma unroll
       for (int l = 0; l < 4; ++l) {
-        const float4 cq = __ldg(rw + l * MB_C);
-        const float T = cubic(cq, t);
-        const float dT = dcubic(cq, t) * x.rd.inv_h;
-        float gT = 0.f;
+        float T[4], dT[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const float4 cq = __ldg(rw + l * MB_C + 32 * jj);
+          T[jj] = cubic(cq, t);
+          dT[jj] = dcubic(cq, t);
+        }
 #pragma unroll
         for (int mm = l * l; mm < (l + 1) * (l + 1); ++mm) {
-          gT = fmaf(g[mm], Y[mm], gT);
-          const float gy = g[mm] * T;
-          gvx = fmaf(gy, J[3 * mm + 0], gvx);
-          gvy = fmaf(gy, J[3 * mm + 1], gvy);
-          gvz = fmaf(gy, J[3 * mm + 2], gvz);
+          float qv = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            qv = fmaf(g[mm][jj], T[jj], qv);
+            gr = fmaf(g[mm][jj] * Y[mm], dT[jj], gr);
+          }
+          Q[mm] = qv;
         }
-        gr = fmaf(gT, dT, gr);
       }
-      gvx = fmaf(gr, su[q][0], gvx);
-      gvy = fmaf(gr, su[q][1], gvy);
-      gvz = fmaf(gr, su[q][2], gvz);
+      gr *= x.rd.inv_h;
+      const float* J = sJ[warp][q];
+      float gvx = gr * su[warp][q][0], gvy = gr * su[warp][q][1], gvz = gr * su[warp][q][2];
+#pragma unroll
+      for (int mm = 0; mm < 16; ++mm) {
+        gvx = fmaf(Q[mm], J[3 * mm + 0], gvx);
+        gvy = fmaf(Q[mm], J[3 * mm + 1], gvy);
+        gvz = fmaf(Q[mm], J[3 * mm + 2], gvz);
+      }
       gvx = warp_sum(gvx);
       gvy = warp_sum(gvy);
       gvz = warp_sum(gvz);
       if (lane == 0) {
-        sred[q][warp][0] = gvx;
-        sred[q][warp][1] = gvy;
-        sred[q][warp][2] = gvz;
+        const float gd = su[warp][q][3];
+        float* pf = ev.PF + 3 * (base + q);
+        pf[0] += gvx + gd * su[warp][q][0];
+        pf[1] += gvy + gd * su[warp][q][1];
+        pf[2] += gvz + gd * su[warp][q][2];
       }
-    }
-    __syncthreads();
-    if (c < n && srow[c] >= 0) {
-      float* pf = ev.PF + 3 * (base + c);
-#pragma unroll
-      for (int d = 0; d < 3; ++d)
-        pf[d] += sred[c][0][d] + sred[c][1][d] + sred[c][2][d] + sred[c][3][d] + sgd[c] * su[c][d];
     }
   }
 }
@@ -439,14 +460,14 @@ using namespace mb;
 extern "C" int mace_b200_edge_l1_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
   if (int rc = edge_args(m, ev, a, b, "edge_l1_fwd")) return rc;
   if (b == a) return 0;
-  k_edge_l1_fwd<128><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  k_edge_l1_fwd<<<(b - a + L1_WARPS - 1) / L1_WARPS, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
   return check_launch("edge_l1_fwd");
 }
 
 extern "C" int mace_b200_edge_l1_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
   if (int rc = edge_args(m, ev, a, b, "edge_l1_bwd")) return rc;
   if (b == a) return 0;
-  k_edge_l1_bwd<64><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  k_edge_l1_bwd<<<(b - a + L1_WARPS - 1) / L1_WARPS, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
   return check_launch("edge_l1_bwd");
 }
 

@@ -184,11 +184,23 @@ extern "C" int mace_b200_timing(int enable, double* ms_out, long long* count_out
 }
 extern "C" const char* mace_b200_last_error(void) { return g_err; }
 
-extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
-  RC(check_pass_args(m, ev, "pass_a"));
+// The chunk's view of the eval struct: with the layer-1 cache, x1 and rho1 live in the cache rows of the chunk.
+static mb_eval_t chunk_view(const mb_eval_t* ev, int a) {
+  mb_eval_t v = *ev;
+  if (ev->x1_cache && ev->rho1_cache) {
+    v.s_x = ev->x1_cache + (size_t)a * 16 * MB_C;
+    v.s_rho = ev->rho1_cache + a;
+  }
+  return v;
+}
+
+extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev_all, void* stream) {
+  RC(check_pass_args(m, ev_all, "pass_a"));
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C;
-  for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
+  for (int a = 0, ci = 0; a < ev_all->nl; a += ev_all->chunk, ++ci) {
+    const mb_eval_t view = chunk_view(ev_all, a);
+    const mb_eval_t* ev = &view;
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
     TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
     RC(x1_gemms(m, ev, a, ci, st));
@@ -199,7 +211,7 @@ extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev, void* 
              ev->H1 + (size_t)a * 4 * C, 4 * C, kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0));
     RC(gb.launch());
   }
-  return readout1(m, ev->H1, ev->eat, ev->nl, st);
+  return readout1(m, ev_all->H1, ev_all->eat, ev_all->nl, st);
 }
 
 extern "C" int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
@@ -282,17 +294,22 @@ extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* 
   return gb.launch();
 }
 
-extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
-  RC(check_pass_args(m, ev, "pass_c"));
+extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev_all, void* stream) {
+  RC(check_pass_args(m, ev_all, "pass_c"));
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C, S = m->S;
   const bool tc = use_tc(m);
+  const bool cached = ev_all->x1_cache && ev_all->rho1_cache;
   static const int offs[4] = {0, 1, 4, 9};
-  for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
+  for (int a = 0, ci = 0; a < ev_all->nl; a += ev_all->chunk, ++ci) {
+    const mb_eval_t view = chunk_view(ev_all, a);
+    const mb_eval_t* ev = &view;
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
     const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
-    TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
-    RC(x1_gemms(m, ev, a, ci, st));
+    if (!cached) {
+      TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
+      RC(x1_gemms(m, ev, a, ci, st));
+    }
     RC(gh1(m, ev->G1 + (size_t)a * 4 * C, ev->s_a, nC, st));
     {
       GemmBatch gb(tc, ev->status, st);   // gA1 = g_h1 Wp1^T

@@ -219,10 +219,16 @@ class ThreePassEngine:
     """The three-pass evaluation on one GPU for a fixed model and species set."""
 
     def __init__(self, model: Mdl.MACEModel, cols, chunk: int = 16384, spline_grid: int = 512, device="cuda",
-                 use_tc: bool | None = None):
+                 use_tc: bool | None = None, x1_cache: bool | None = None):
         self.device = torch.device(device)
         self.model = model
         self.chunk = int(chunk)
+        # cache pass A's layer-1 intermediates for pass C when they fit comfortably (8 KB per local atom); None = auto
+        env = os.environ.get("MACE_B200_X1_CACHE")
+        self.x1_cache = x1_cache if x1_cache is not None else (None if env is None else env != "0")
+        self.graphs = os.environ.get("MACE_B200_GRAPHS", "0") == "1"
+        self._graph = None
+        self.captures = 0
         self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device, use_tc=use_tc)
         Zn = len(model.arch.atomic_numbers)
         col2s = torch.full((Zn,), -1, dtype=torch.int64)
@@ -255,10 +261,22 @@ class ThreePassEngine:
                  s_gh=self._get("s_gh", (ch, C), f32), s_sc=self._get("s_sc", (ch, C), f32),
                  s_rho=self._get("s_rho", (ch,), f32), s_grho=self._get("s_grho", (ch,), f32),
                  status=self._get("status", (1,), torch.int32))
+        if self._use_x1_cache(nl):
+            b["x1_cache"] = self._get("x1_cache", (max(nl, 1), 16, C), f32)
+            b["rho1_cache"] = self._get("rho1_cache", (max(nl, 1),), f32)
         ev = N.MBEval(nl=nl, nt=nt, P=P, pair_i=N.ptr(plan.pi), pair_j=N.ptr(plan.pj), rij=N.ptr(plan.rij),
                       rowptr=N.ptr(plan.rowptr), spec=N.ptr(plan.spec), chunk=ch, order=N.ptr(plan.order),
                       spec_off=plan.spec_off.ctypes.data, **{k: N.ptr(v) for k, v in b.items()})
         return ev, b
+
+    def _use_x1_cache(self, nl: int) -> bool:
+        if self.x1_cache is not None:
+            return bool(self.x1_cache)
+        have = self._buf.get("x1_cache")
+        if have is not None and have.numel() >= nl * 16 * C:
+            return True
+        free, _total = torch.cuda.mem_get_info(self.device)
+        return nl * 16 * C * 4 < 0.25 * free
 
     def _check_status(self, b, what):
         s = int(b["status"].item())
@@ -270,13 +288,10 @@ class ThreePassEngine:
             raise RuntimeError(f"mace_b200 {what}: input error reported by the kernels: {', '.join(names)}")
 
     # ------------------------------------------------------------------------------------------------ evaluation
-    def evaluate(self, plan: Plan, forward_exchange=None, reverse_exchange=None, check: bool = True):
-        """(eatoms fp64 [nl], pair forces dE/drij fp64 [P, 3] in the caller's pair order) on the device.
-        forward_exchange(H1 [nt, 512]) fills ghost rows from their owners; reverse_exchange(G1 [nt, 512]) adds
-        ghost rows onto their owners (both in place; None when nt == nl)."""
+    def _run(self, plan, ev, b, forward_exchange=None, reverse_exchange=None):
+        """The device work of one evaluation on the current stream (capturable when there is no exchange)."""
         L = N.lib()
         m = N.byref(self.fm.struct)
-        ev, b = self.eval_struct(plan)
         evp = N.byref(ev)
         st = torch.cuda.current_stream(self.device).cuda_stream
         b["status"].zero_()
@@ -293,11 +308,63 @@ class ThreePassEngine:
         fbits = self._get("fmax", (1,), torch.int32)
         fbits.zero_()
         N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
+        return PFd, fbits
+
+    def evaluate(self, plan: Plan, forward_exchange=None, reverse_exchange=None, check: bool = True,
+                 graph: bool | None = None):
+        """(eatoms fp64 [nl], pair forces dE/drij fp64 [P, 3] in the caller's pair order) on the device.
+        forward_exchange(H1 [nt, 512]) fills ghost rows from their owners; reverse_exchange(G1 [nt, 512]) adds
+        ghost rows onto their owners (both in place; None when nt == nl).  graph=True (or engine.graphs) replays
+        the whole evaluation as one captured CUDA graph when there is no exchange to run between the passes."""
+        use_graph = self.graphs if graph is None else graph
+        if use_graph and forward_exchange is None and reverse_exchange is None:
+            b, PFd, fbits = self._evaluate_graph(plan)
+        else:
+            ev, b = self.eval_struct(plan)
+            PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange)
         self._last = b
         if check:
             self._check_status(b, "evaluation")
         self.fmax = float(fbits.view(torch.float32).item()) if check else None
         return b["eat"][:plan.nl], PFd
+
+    # ------------------------------------------------------------------------------------------------ CUDA graph
+    _STAGED = ("pi", "pj", "rij", "rowptr", "spec", "order")
+
+    def _evaluate_graph(self, plan: Plan):
+        """Capture (once per shape / species layout) and replay the evaluation.  The plan's device arrays are copied
+        into persistent staging buffers whose addresses the graph holds; the species segment table (host) is part of
+        the capture key because the chunk loops bake it into the launch parameters."""
+        key = (plan.P, plan.nl, plan.nt, plan.perm is not None, plan.spec_off.tobytes())
+        g = self._graph
+        if g is None or g["key"] != key:
+            self._graph = None
+            staged = Plan.__new__(Plan)
+            staged.P, staged.nl, staged.nt, staged.n_chunks = plan.P, plan.nl, plan.nt, plan.n_chunks
+            staged.spec_off = plan.spec_off.copy()
+            for name in self._STAGED:
+                setattr(staged, name, getattr(plan, name).clone())
+            staged.perm = None if plan.perm is None else plan.perm.clone()
+            ev, b = self.eval_struct(staged)
+            self._run(staged, ev, b)                            # eager warm-up (one-time kernel attributes)
+            torch.cuda.synchronize(self.device)
+            gr = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(gr, stream=side):
+                    PFd, fbits = self._run(staged, ev, b)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            g = self._graph = dict(key=key, graph=gr, staged=staged, ev=ev, b=b, PFd=PFd, fbits=fbits)
+            self.captures += 1
+        else:
+            st = g["staged"]
+            for name in self._STAGED:
+                getattr(st, name).copy_(getattr(plan, name), non_blocking=True)
+            if plan.perm is not None:
+                st.perm.copy_(plan.perm, non_blocking=True)
+        g["graph"].replay()
+        return g["b"], g["PFd"], g["fbits"]
 
     def owner_exchange(self, owner, nl: int):
         """Exchange callbacks for ghosts given by an owner map (owner[j] = local owner of atom j for j >= nl): the

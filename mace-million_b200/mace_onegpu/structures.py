@@ -13,7 +13,8 @@ import numpy as np
 
 WATER_SPACING = 3.104
 ALLOY_Z = (3, 8, 11, 12, 13, 14, 16, 20, 22, 26, 27, 28, 29, 30, 40, 42)
-MASS = {1: 1.008, 8: 15.999}
+MASS = {1: 1.008, 3: 6.94, 8: 15.999, 11: 22.990, 12: 24.305, 13: 26.982, 14: 28.085, 16: 32.06, 20: 40.078,
+        22: 47.867, 26: 55.845, 27: 58.933, 28: 58.693, 29: 63.546, 30: 65.38, 40: 91.224, 42: 95.95}   # amu
 
 
 def _random_rotations(rng: np.random.Generator, n: int) -> np.ndarray:
@@ -65,7 +66,7 @@ def species_columns(Z, atomic_numbers) -> np.ndarray:
 def maxwell_boltzmann(Z, temperature: float, seed: int = 0) -> np.ndarray:
     """Velocities (A/fs) at the given temperature with zero total momentum."""
     kB = 8.617333262e-5                                    # eV / K
-    amu = 1.0364269e-4                                     # eV fs^2 / A^2 per amu
+    amu = 103.6427                                         # 1 amu A^2 / fs^2 = 103.6427 eV
     m = np.array([MASS.get(int(z), 2.0 * int(z)) for z in Z]) * amu
     rng = np.random.default_rng(seed)
     v = rng.normal(size=(len(Z), 3)) * np.sqrt(kB * temperature / m)[:, None]

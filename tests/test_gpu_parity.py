@@ -147,3 +147,34 @@ def test_ghost_exchange_gpu(mdl, water, oracle):
     eat, pf, _ = _run(_engine(mdl, water["cols"], 64), water, owner=owner, nt=len(owner), pj=pj2)
     assert (eat - oracle["eat"]).abs().max() < E_TOL
     assert (pf - oracle["pf"]).abs().max() < F_TOL
+
+
+def test_x1_cache_is_bitwise_identical(mdl, water):
+    """Pass C reading pass A's cached layer-1 intermediates gives the recomputing schedule's results: energies
+    bitwise, pair forces to fp32 summation order (dE/dX2 is scattered with atomics, so G1 is only reproducible to
+    the last bits between any two evaluations)."""
+    cols = sorted(set(int(c) for c in water["cols"]))
+    out = []
+    for cache in (False, True):
+        eng = E.ThreePassEngine(mdl, cols, chunk=64, device="cuda", x1_cache=cache)
+        plan = eng.plan(water["pi"], water["pj"], water["rij"], torch.as_tensor(water["cols"]), water["n"], water["n"])
+        eat, pf = eng.evaluate(plan)
+        out.append((eat.clone(), pf.clone()))
+    assert torch.equal(out[0][0], out[1][0])
+    assert (out[0][1] - out[1][1]).abs().max().item() < 1e-5
+
+
+def test_cuda_graph_replay_matches_eager(mdl, water):
+    """The evaluation captured as one CUDA graph and replayed (twice, the second time with freshly built plan
+    arrays copied into the staging buffers) gives the eager results (energies bitwise, pair forces to fp32
+    summation order of the atomic dE/dX2 scatter)."""
+    cols = sorted(set(int(c) for c in water["cols"]))
+    eng = E.ThreePassEngine(mdl, cols, chunk=64, device="cuda")
+    mk = lambda: eng.plan(water["pi"], water["pj"], water["rij"], torch.as_tensor(water["cols"]), water["n"],
+                          water["n"])
+    e0, p0 = eng.evaluate(mk(), graph=False)
+    e0, p0 = e0.clone(), p0.clone()
+    for _ in range(2):
+        e1, p1 = eng.evaluate(mk(), graph=True)
+        assert torch.equal(e0, e1) and (p0 - p1).abs().max().item() < 1e-5
+    assert eng.captures == 1
