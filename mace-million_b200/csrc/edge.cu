@@ -93,6 +93,22 @@ __device__ __forceinline__ float block_sum128(float v, float* red4) {
   return red4[0] + red4[1] + red4[2] + red4[3];
 }
 
+// Warp-wide sums of 16 per-lane values with 16 shuffles: each step exchanges half of the remaining values with the
+// partner lane of one bit, so that lane L ends with the sum over the warp of v[L >> 1].
+__device__ __forceinline__ float transpose_reduce16(float* v, int lane) {
+#pragma unroll
+  for (int h = 8, bit = 16; h >= 1; h >>= 1, bit >>= 1) {
+    const bool up = lane & bit;
+#pragma unroll
+    for (int q = 0; q < h; ++q) {
+      const float send = up ? v[q] : v[q + h];
+      const float keep = up ? v[q + h] : v[q];
+      v[q] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
 // ------------------------------------------------------------------------------------------------ layer 1
 // Layer-1 edge kernels (pass A / C forward: s_msg[i][lm][c] = sum_e T1(r_e; pair_e)[l][c] Y_e[lm], s_rho[i];
 // pass C backward: PF[e] += dL/dv_e from g = dL/dmsg1 in s_msg and s_grho): one warp per receiver, lane = channels lane + 32 j (j = 0..3, so every load and store
@@ -100,6 +116,9 @@ __device__ __forceinline__ float block_sum128(float v, float* red4) {
 // into warp-private shared memory; 4 receivers per CTA, no CTA-wide barrier.  The backward forms per lane
 // Q[lm] = sum_{its 4 channels} g[lm][c] T[l][c] and contracts it with the SH Jacobian once per 4 channels.
 constexpr int L1_WARPS = 4;
+#ifndef MB_L1_BWD_MINB
+#define MB_L1_BWD_MINB 4
+#endif
 
 __global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_fwd(const mb_model_t m, const mb_eval_t ev, int a, int b) {
   __shared__ __align__(16) float sY[L1_WARPS][32][16];
@@ -174,10 +193,12 @@ __global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_fwd(const mb_model_t 
   if (lane == 0) ev.s_rho[il] = rho;
 }
 
-__global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_bwd(const mb_model_t m, const mb_eval_t ev, int a, int b) {
+__global__ void __launch_bounds__(32 * L1_WARPS, MB_L1_BWD_MINB) k_edge_l1_bwd(const mb_model_t m, const mb_eval_t ev,
+                                                                              int a, int b) {
   __shared__ __align__(16) float sY[L1_WARPS][32][16];
-  __shared__ __align__(16) float sJ[L1_WARPS][32][48];
-  __shared__ float su[L1_WARPS][32][4];
+  __shared__ __align__(16) float sred[L1_WARPS][32][17];
+  __shared__ __align__(16) float sv[L1_WARPS][32][4];
+  __shared__ float sgd[L1_WARPS][32];
   __shared__ int srow[L1_WARPS][32];
   __shared__ float st[L1_WARPS][32];
   const EdgeCtx x = make_ctx(m, ev);
@@ -209,14 +230,14 @@ __global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_bwd(const mb_model_t 
         row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
         st[warp][lane] = t;
         const float ir = 1.f / r;
-        float3 u = make_float3(v.x * ir, v.y * ir, v.z * ir);
-        sh_jacobian(u, r, sY[warp][lane], sJ[warp][lane]);
+        sh16<float>(v.x * ir, v.y * ir, v.z * ir, sY[warp][lane]);
         float ed, ded;
         edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
-        su[warp][lane][0] = u.x;
-        su[warp][lane][1] = u.y;
-        su[warp][lane][2] = u.z;
-        su[warp][lane][3] = grho * ded;
+        sv[warp][lane][0] = v.x;
+        sv[warp][lane][1] = v.y;
+        sv[warp][lane][2] = v.z;
+        sv[warp][lane][3] = r;
+        sgd[warp][lane] = grho * ded;
       }
       srow[warp][lane] = row;
     }
@@ -232,16 +253,17 @@ __global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_bwd(const mb_model_t 
         const float4 y4 = *reinterpret_cast<const float4*>(&sY[warp][q][k]);
         Y[k] = y4.x; Y[k + 1] = y4.y; Y[k + 2] = y4.z; Y[k + 3] = y4.w;
       }
+      // Q[lm] = sum_c g[lm][c] T_l[c] (dE/dY, slot 0 unused: Y[0] is constant);  G_l[c] = sum_{m in l} g Y = dE/dT_l[c]
       float Q[16];
-      float gr = 0.f;
+      float Sb = 0.f, Sc = 0.f, Sd = 0.f;
 #pragma unroll
       for (int l = 0; l < 4; ++l) {
-        float T[4], dT[4];
+        float4 cq[4];
+        float T[4], G[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-          const float4 cq = __ldg(rw + l * MB_C + 32 * jj);
-          T[jj] = cubic(cq, t);
-          dT[jj] = dcubic(cq, t);
+          cq[jj] = __ldg(rw + l * MB_C + 32 * jj);
+          T[jj] = cubic(cq[jj], t);
         }
 #pragma unroll
         for (int mm = l * l; mm < (l + 1) * (l + 1); ++mm) {
@@ -249,39 +271,56 @@ __global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_bwd(const mb_model_t 
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             qv = fmaf(g[mm][jj], T[jj], qv);
-            gr = fmaf(g[mm][jj] * Y[mm], dT[jj], gr);
+            G[jj] = fmaf(g[mm][jj], Y[mm], G[jj]);
           }
           Q[mm] = qv;
         }
-      }
-      gr *= x.rd.inv_h;
-      const float* J = sJ[warp][q];
-      float gvx = gr * su[warp][q][0], gvy = gr * su[warp][q][1], gvz = gr * su[warp][q][2];
 #pragma unroll
-      for (int mm = 0; mm < 16; ++mm) {
-        gvx = fmaf(Q[mm], J[3 * mm + 0], gvx);
-        gvy = fmaf(Q[mm], J[3 * mm + 1], gvy);
-        gvz = fmaf(Q[mm], J[3 * mm + 2], gvz);
+        for (int jj = 0; jj < 4; ++jj) {
+          Sb = fmaf(G[jj], cq[jj].y, Sb);
+          Sc = fmaf(G[jj], cq[jj].z, Sc);
+          Sd = fmaf(G[jj], cq[jj].w, Sd);
+        }
       }
-      gvx = warp_sum(gvx);
-      gvy = warp_sum(gvy);
-      gvz = warp_sum(gvz);
-      if (lane == 0) {
-        const float gd = su[warp][q][3];
-        float* pf = ev.PF + 3 * (base + q);
-        pf[0] += gvx + gd * su[warp][q][0];
-        pf[1] += gvy + gd * su[warp][q][1];
-        pf[2] += gvz + gd * su[warp][q][2];
+      Q[0] = fmaf(t, fmaf(3.f * t, Sd, 2.f * Sc), Sb);   // dE/dt of this lane's channels
+      const float s = transpose_reduce16(Q, lane);
+      if ((lane & 1) == 0) sred[warp][q][lane >> 1] = s;
+    }
+    __syncwarp();
+    if (lane < n && srow[warp][lane] >= 0) {
+      const float* gs = sred[warp][lane];
+      const float r = sv[warp][lane][3], ir = 1.f / r;
+      const float3 u = make_float3(sv[warp][lane][0] * ir, sv[warp][lane][1] * ir, sv[warp][lane][2] * ir);
+      float Yj[16], J[48];
+      sh_jacobian(u, r, Yj, J);
+      const float gr = fmaf(gs[0], x.rd.inv_h, sgd[warp][lane]);
+      float f[3] = {gr * u.x, gr * u.y, gr * u.z};
+#pragma unroll
+      for (int mm = 1; mm < 16; ++mm) {
+        f[0] = fmaf(gs[mm], J[3 * mm + 0], f[0]);
+        f[1] = fmaf(gs[mm], J[3 * mm + 1], f[1]);
+        f[2] = fmaf(gs[mm], J[3 * mm + 2], f[2]);
       }
+      float* pf = ev.PF + 3 * (base + lane);
+#pragma unroll
+      for (int d = 0; d < 3; ++d) pf[d] += f[d];
     }
   }
 }
 
 // ------------------------------------------------------------------------------------------------ layer 2 forward
-// s_msg[i][o][c] = sum_e sum_t coef_t W2(r_e)[w_t][c] X2[j_e][k_t][c] Y_e[m_t];  s_rho[i]
+// Resident CTAs per SM the layer-2 kernels are compiled for (register budget 65536 / (128 x MINB) per thread).
+#ifndef MB_L2_FWD_MINB
+#define MB_L2_FWD_MINB 5
+#endif
+#ifndef MB_L2_BWD_MINB
+#define MB_L2_BWD_MINB 4
+#endif
+
+// s_msg[i][o][c] = sum_e sum_(w,k) W2(r_e)[w][c] X2[j_e][k][c] by_e[(w,k,o)];  s_rho[i]
 template <int EB>
-__global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
-  __shared__ __align__(16) float scy[EB][TP2_NT_PAD];
+__global__ void __launch_bounds__(128, MB_L2_FWD_MINB) k_edge_l2_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
+  __shared__ __align__(16) float sby[EB][TP2_NB_PAD];
   __shared__ int srow[EB];
   __shared__ int ssend[EB];
   __shared__ float st[EB];
@@ -313,7 +352,7 @@ __global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const m
         const float ir = 1.f / r;
         float Y[16];
         sh16<float>(v.x * ir, v.y * ir, v.z * ir, Y);
-        tp2_cy(Y, scy[c]);
+        tp2_by(Y, sby[c]);
         float ed, ded;
         edge_density(r, m.wd2, x.rd.r_max, x.rd.p, ed, ded);
         rho += ed;
@@ -328,7 +367,7 @@ __global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const m
       float X[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) X[k] = __ldg(xs + k * MB_C);
-      tp2_fwd(tab + row + c, st[q], X, scy[q], acc);
+      tp2_fwd(tab + row + c, st[q], X, sby[q], acc);
     }
   }
   float* out = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;
@@ -340,28 +379,32 @@ __global__ void __launch_bounds__(128) k_edge_l2_fwd(const mb_model_t m, const m
 
 // ------------------------------------------------------------------------------------------------ layer 2 backward
 // Pass B: given g = dE/dmsg2 (s_msg, [i][40][C]) and s_grho: PF[e] += dE/dv_e, GX2[j_e] += dE/dX2.
-// Per receiver and channel the products cg = coef * g[o] live in registers (tp2_cg); per edge the 16 SH values are
-// read once from shared memory.
+// Per receiver and channel the collapsed coefficients A = sum_o coef g[o] live in registers (tp2_a).  Per (edge,
+// channel) the kernel forms dE/dY[1..15] and dE/dt (slot 0, Y[0] being constant); the 16 values are summed over the
+// warp (transpose_reduce16) and over the 4 warps in shared memory, and one thread per edge applies the SH Jacobian
+// and the spline's 1/h once.
 template <int EB>
-__global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const mb_eval_t ev, int a) {
+__global__ void __launch_bounds__(128, MB_L2_BWD_MINB) k_edge_l2_bwd(const mb_model_t m, const mb_eval_t ev, int a) {
   __shared__ __align__(16) float sY[EB][16];
-  __shared__ __align__(16) float sJ[EB][48];
-  __shared__ float su[EB][3];
+  __shared__ __align__(16) float sv[EB][4];
+  __shared__ __align__(16) float sred[EB][4 * 16 + 4];   // per edge: 4 warps x 16 slots, padded (bank spread)
   __shared__ float sgd[EB];
   __shared__ int srow[EB];
   __shared__ int ssend[EB];
   __shared__ float st[EB];
-  __shared__ float sred[EB][4][3];
   const EdgeCtx x = make_ctx(m, ev);
   const int il = blockIdx.x, i = a + il, c = threadIdx.x, warp = c >> 5, lane = c & 31;
   int64_t e0, e1;
   if (!row_range(ev, i, e0, e1)) return;
   const float4* tab = reinterpret_cast<const float4*>(m.tab2);
-  float g[TP2_NO], cg[TP2_NCG];
-  const float* gin = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;
+  float A[TP2_NA];
+  {
+    float g[TP2_NO];
+    const float* gin = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;
 #pragma unroll
-  for (int q = 0; q < TP2_NO; ++q) g[q] = gin[q * MB_C];
-  tp2_cg(g, cg);
+    for (int q = 0; q < TP2_NO; ++q) g[q] = gin[q * MB_C];
+    tp2_a(g, A);
+  }
   const float grho = ev.s_grho[il];
   for (int64_t base = e0; base < e1; base += EB) {
     const int n = (int)min((int64_t)EB, e1 - base);
@@ -379,11 +422,11 @@ __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const m
         st[c] = t;
         ssend[c] = j;
         const float ir = 1.f / r;
-        float3 u = make_float3(v.x * ir, v.y * ir, v.z * ir);
-        sh_jacobian(u, r, sY[c], sJ[c]);
-        su[c][0] = u.x;
-        su[c][1] = u.y;
-        su[c][2] = u.z;
+        sh16<float>(v.x * ir, v.y * ir, v.z * ir, sY[c]);
+        sv[c][0] = v.x;
+        sv[c][1] = v.y;
+        sv[c][2] = v.z;
+        sv[c][3] = r;
         float ed, ded;
         edge_density(r, m.wd2, x.rd.r_max, x.rd.p, ed, ded);
         sgd[c] = grho * ded;
@@ -395,6 +438,7 @@ __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const m
       const int row = srow[q];
       if (row < 0) continue;
       const int j = ssend[q];
+      const float t = st[q];
       const float* xs = ev.X2 + (size_t)j * 4 * MB_C + c;
       float X[4], gX[4] = {0.f, 0.f, 0.f, 0.f}, gY[16], Y[16];
 #pragma unroll
@@ -408,34 +452,49 @@ __global__ void __launch_bounds__(128) k_edge_l2_bwd(const mb_model_t m, const m
         Y[k + 3] = y4.w;
         gY[k] = gY[k + 1] = gY[k + 2] = gY[k + 3] = 0.f;
       }
-      float gr = 0.f;
-      tp2_bwd(tab + row + c, st[q], x.rd.inv_h, X, Y, g, cg, gX, gY, gr);
+      float Sb = 0.f, Sc = 0.f, Sd = 0.f;
+      tp2_bwd(tab + row + c, t, X, Y, A, gX, gY, Sb, Sc, Sd);
       float* gxo = ev.GX2 + (size_t)j * 4 * MB_C + c;
 #pragma unroll
       for (int k = 0; k < 4; ++k) atomicAdd(gxo + k * MB_C, gX[k]);
-      const float* J = sJ[q];
-      float gvx = gr * su[q][0], gvy = gr * su[q][1], gvz = gr * su[q][2];
-#pragma unroll
-      for (int mm = 0; mm < 16; ++mm) {
-        gvx = fmaf(gY[mm], J[3 * mm + 0], gvx);
-        gvy = fmaf(gY[mm], J[3 * mm + 1], gvy);
-        gvz = fmaf(gY[mm], J[3 * mm + 2], gvz);
-      }
-      gvx = warp_sum(gvx);
-      gvy = warp_sum(gvy);
-      gvz = warp_sum(gvz);
-      if (lane == 0) {
-        sred[q][warp][0] = gvx;
-        sred[q][warp][1] = gvy;
-        sred[q][warp][2] = gvz;
-      }
+      gY[0] = fmaf(t, fmaf(3.f * t, Sd, 2.f * Sc), Sb);
+      const float s = transpose_reduce16(gY, lane);
+      if ((lane & 1) == 0) sred[q][warp * 16 + (lane >> 1)] = s;
     }
     __syncthreads();
     if (c < n && srow[c] >= 0) {
+      float gs[16];
+#pragma unroll
+      for (int k = 0; k < 16; k += 4) {
+        float4 acc4 = *reinterpret_cast<const float4*>(&sred[c][k]);
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+          const float4 o4 = *reinterpret_cast<const float4*>(&sred[c][w * 16 + k]);
+          acc4.x += o4.x;
+          acc4.y += o4.y;
+          acc4.z += o4.z;
+          acc4.w += o4.w;
+        }
+        gs[k] = acc4.x;
+        gs[k + 1] = acc4.y;
+        gs[k + 2] = acc4.z;
+        gs[k + 3] = acc4.w;
+      }
+      const float r = sv[c][3], ir = 1.f / r;
+      const float3 u = make_float3(sv[c][0] * ir, sv[c][1] * ir, sv[c][2] * ir);
+      float Yj[16], J[48];
+      sh_jacobian(u, r, Yj, J);
+      const float gr = fmaf(gs[0], x.rd.inv_h, sgd[c]);
+      float f[3] = {gr * u.x, gr * u.y, gr * u.z};
+#pragma unroll
+      for (int mm = 1; mm < 16; ++mm) {
+        f[0] = fmaf(gs[mm], J[3 * mm + 0], f[0]);
+        f[1] = fmaf(gs[mm], J[3 * mm + 1], f[1]);
+        f[2] = fmaf(gs[mm], J[3 * mm + 2], f[2]);
+      }
       float* pf = ev.PF + 3 * (base + c);
 #pragma unroll
-      for (int d = 0; d < 3; ++d)
-        pf[d] += sred[c][0][d] + sred[c][1][d] + sred[c][2][d] + sred[c][3][d] + sgd[c] * su[c][d];
+      for (int d = 0; d < 3; ++d) pf[d] += f[d];
     }
   }
 }
