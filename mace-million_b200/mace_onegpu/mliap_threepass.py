@@ -6,7 +6,7 @@ same module path (pickles made with either resolve to this class), constructor s
 data.update_pair_forces_gpu in the caller's pair order), H1 forward / G1 reverse exchange through
 data.forward_exchange / data.reverse_exchange with the same 2^31-element column split, the same guards
 (int32 neighbour-slot estimate, non-finite / absurd force abort) and the same MACE3P_* environment knobs that still
-mean something (CHUNK, LOG, SKIN, ALLOW_HUGE, FMAX_ABORT).
+mean something (CHUNK, LOG, SKIN, ALLOW_HUGE, FMAX_ABORT, GRAPHS).
 
 Per call: pass A (layer-1 features of every local atom) -> forward exchange -> pass B (layer-2 energy, pair forces,
 G1 = dE2/dh1) -> reverse exchange -> pass C (loss E1 + G1 . h1, remaining pair forces); all arithmetic runs in the
@@ -87,6 +87,10 @@ class ThreePassMLIAP(MLIAPUnified):
         self._cols = cols
         self._eng = ThreePassEngine(self.model, cols, chunk=self.chunk, spline_grid=self.spline_grid or 512,
                                     device=dev)
+        # MACE3P_GRAPHS=1 (mliap_threepass.py:255): replay the evaluation as one CUDA graph; the engine captures only
+        # when no exchange has to run between the passes (one rank without ghosts)
+        if os.environ.get("MACE3P_GRAPHS", "0") == "1":
+            self._eng.graphs = True
         self._fmax_abort = float(os.environ.get("MACE3P_FMAX_ABORT", "100.0"))
         path = os.environ.get("MACE3P_LOG")
         self._log = open(path, "a", buffering=1) if path else None
