@@ -130,12 +130,12 @@ const char* mace_b200_last_error(void);
 int mace_b200_struct_sizes(int32_t* model_bytes, int32_t* eval_bytes);
 /* Number of kernels this library has launched since it was loaded (all threads). */
 unsigned long long mace_b200_launch_count(void);
-/* Per-kind CUDA-event timing of the pass runners' edge and symmetric-contraction launches (the reference's
+/* Per-kind CUDA-event timing of the pass runners' edge, symmetric-contraction and grouped node-GEMM launches (the reference's
  * per-pass wall timers, mliap_threepass.py:525-585, at kernel granularity).  mace_b200_timing(enable, ms, cnt)
  * synchronises on the recorded events, writes the accumulated milliseconds and launch counts per kind
  * (MB_K_*, arrays of MB_NKINDS, either may be null), resets them and switches recording on or off. */
 enum { MB_K_EDGE_L1_FWD = 0, MB_K_EDGE_L1_BWD = 1, MB_K_EDGE_L2_FWD = 2, MB_K_EDGE_L2_BWD = 3, MB_K_SYMCON = 4,
-       MB_NKINDS = 5 };
+       MB_K_NODE_GEMM = 5, MB_NKINDS = 6 };
 int mace_b200_timing(int enable, double* ms_out, long long* count_out);
 /* FP32 FFMA issue ceiling of the current device (TFLOP/s), by an 8-chain FFMA kernel on 8 CTAs per SM (the edge
  * kernels' roofline denominator; scratch is one device float). */
@@ -208,7 +208,10 @@ int mace_b200_node_gemm(const float* X, int64_t ldx, const int32_t* xoff, int32_
                         const float* rho, int32_t accumulate, void* stream);
 
 /* The same GEMM on the 5th-generation tensor cores (tcgen05.mma kind::tf32, accumulator in TMEM), 3xTF32:
- * Bt_split = [2][n_seg][128 n][128 k] (K-major B, tf32 hi plane then lo plane, plane = elements per plane).
+ * Bt_split = [2][n_seg][128 x 128] (K-major B split into a tf32 hi plane then a lo plane, plane = elements per
+ * plane; every 128 x 128 matrix permuted into four 16 KB K blocks in the SWIZZLE_128B shared-memory image:
+ * element (n, k) at (k / 32) * 4096 + (n / 8) * 256 + (n % 8) * 32 + (((k % 32) / 4) ^ (n % 8)) * 4 + k % 4).
+ * X, Y, Bt_split 16-byte aligned.  Persistent kernel, one CTA per SM. 
  * A timeout of its bounded MMA-barrier wait sets MB_ST_TC_TIMEOUT in *status (may be null). */
 int mace_b200_node_gemm_tc(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg, const float* Bt_split,
                            int64_t plane, float* Y, int64_t ldy, int32_t yoff, int32_t mult, const int32_t* order,

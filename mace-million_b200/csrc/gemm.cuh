@@ -41,6 +41,8 @@ __device__ __forceinline__ int gemm_problem_of(const GemmGroup& grp, int tile) {
 }
 
 int gemm_group_launch_simt(const GemmGroup& grp, cudaStream_t st);
+void timer_begin(int kind, cudaStream_t st, int* slot);   // per-kind CUDA-event timing (passes.cu)
+void timer_end(int slot, cudaStream_t st);
 int gemm_group_launch_tc(const GemmGroup& grp, cudaStream_t st);
 
 // Host-side builder: add problems, launch once (flushes automatically when full).
@@ -85,7 +87,10 @@ struct GemmBatch {
 
   int launch() {
     if (g.n == 0) return 0;
+    int slot;
+    timer_begin(MB_K_NODE_GEMM, st, &slot);
     int rc = tc ? gemm_group_launch_tc(g, st) : gemm_group_launch_simt(g, st);
+    timer_end(slot, st);
     g.n = 0;
     return rc;
   }

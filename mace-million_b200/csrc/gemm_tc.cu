@@ -1,25 +1,47 @@
 // Node GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulator), 3xTF32 for fp32-level accuracy:
 //   Y[atom][yoff + m][:] (+)= alpha_atom * sum_s X[atom][xoff_s + m][:] @ B_s
-// with A = X rows gathered per (atom, m) and B given K-major and pre-split on the host into tf32 hi / lo planes
-// (Bt[n][k], plane stride `plane`).  A is split on the fly: a_hi = rna_tf32(a), a_lo = rna_tf32(a - a_hi), and
-// D = a_hi b_hi + a_hi b_lo + a_lo b_hi accumulates in fp32 in TMEM (the lo*lo term, ~2^-22 relative, is dropped).
+// with A = X rows gathered per (atom, m) and B given as tf32 hi / lo planes, every 128 x 128 matrix stored as four
+// 16 KB K blocks that are already in the SWIZZLE_128B K-major shared-memory image (host: engine.tc_planes).  A is
+// split on the fly: a_hi = rna_tf32(a), a_lo = rna_tf32(a - a_hi), and D = a_hi b_hi + a_hi b_lo + a_lo b_hi
+// accumulates in fp32 in TMEM (the lo*lo term, ~2^-22 relative, is dropped).
 //
-// CTA: 256 threads, tile 128 rows x 128 columns, K blocks of 32 (one 128-byte SWIZZLE_128B atom of tf32 per row),
-// two smem stages (A hi/lo + B hi/lo = 64 KB each) released by tcgen05.commit -> mbarrier.  One thread issues the
-// MMAs (M = 128, N = 128, K = 8 per instruction, cta_group::1); the epilogue reads TMEM with tcgen05.ld 32x32b.
-// Every mbarrier wait is bounded: on expiry the kernel records MB_ST_TC_TIMEOUT in the status word, still waits
-// (bounded) for its own MMAs, frees its TMEM and exits without writing.
+// Persistent, warp-specialised CTA (one per SM, 288 threads), static round-robin over the 128-row tiles of all
+// problems of the group:
+//   warps 0-3  producers: thread p owns row p of the tile.  Its 128-byte slice of each K block is prefetched
+//              TC_RAW blocks ahead with cp.async into a padded raw ring (no registers held), then split into
+//              tf32 hi / lo and stored into the swizzled operand stage; thread 0 also fetches the stage's B hi / lo
+//              blocks with two 16 KB cp.async.bulk copies (no multicast).
+//   warp 8     barrier init, TMEM allocation (two 128-column accumulators) and, on lane 0, the MMA issue:
+//              12 tcgen05.mma kind::tf32 (M = N = 128, K = 8) per K block, tcgen05.commit -> stage-empty barrier,
+//              and after a tile's last block -> accumulator-full barrier.
+//   warps 4-7  epilogue: tcgen05.ld 32x32b of the finished accumulator (warp w reads TMEM lanes 32 (w % 4) ..,
+//              one row per lane), row scale 1 / (rho + 1), then a transpose through shared memory so that the
+//              optional accumulate load and the store of every 32-column chunk go out as full 128-byte row
+//              segments (4 rows per warp instruction); then release the accumulator.
+// The two accumulators let a tile's epilogue overlap the next tile's K loop.  Every mbarrier wait is bounded: on
+// expiry the kernel records MB_ST_TC_TIMEOUT, every role stops, outstanding copies and MMAs are drained (bounded),
+// the TMEM is freed and the kernel exits (outputs of unfinished tiles are not written).
 #include "gemm.cuh"
 
 namespace mb {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32;
-constexpr int TC_THREADS = 256;
-constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 4;          // 16 KB per operand plane
-constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;          // A hi, A lo, B hi, B lo
-constexpr int TC_STAGES = 2;
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 64;   // + alignment slack + barriers
-constexpr unsigned long long TC_WAIT_LIMIT = 1ull << 26;  // try_wait iterations before giving up
+constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 4;          // 16 KB: one operand plane of one K block
+constexpr int TC_STAGES = 2;                               // operand stages (A hi, A lo, B hi, B lo)
+constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;
+constexpr int TC_RAW = 4;                                  // cp.async depth of the raw A ring, in K blocks
+constexpr int TC_RAW_ROW = 144;                            // one row's 128-byte K slice + 16 bytes of bank padding
+constexpr int TC_RAW_BYTES = TC_BM * TC_RAW_ROW;
+constexpr int TC_EPI_ROW = 33;                             // epilogue transpose: 32 floats per row + 1 (bank spread)
+constexpr int TC_EPI_BYTES = 4 * 32 * TC_EPI_ROW * 4;      // one 32-row x 32-column chunk per epilogue warp
+constexpr int TC_THREADS = 288;                            // 4 producer warps, 4 epilogue warps, 1 MMA warp
+constexpr int TC_MMA_WARP = 8;
+constexpr int TC_ACC_COLS = 2 * TC_BN;
+constexpr int TC_RAW_OFF = TC_STAGES * TC_STAGE_BYTES;
+constexpr int TC_EPI_OFF = TC_RAW_OFF + TC_RAW * TC_RAW_BYTES;
+constexpr int TC_BAR_OFF = TC_EPI_OFF + TC_EPI_BYTES;
+constexpr int TC_SMEM = TC_BAR_OFF + 256 + 1024;           // + barriers / TMEM slot / flag + alignment slack
+constexpr unsigned long long TC_WAIT_LIMIT = 1ull << 26;  // try_wait polls before giving up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -72,6 +94,14 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
 // Bounded wait for the phase with the given parity; returns false when the limit expired.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
@@ -89,185 +119,315 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ GemmGroup grp) {
+// global -> this CTA's shared memory, completing on an mbarrier transaction count (16-byte aligned, bytes % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+struct TcBars {
+  uint64_t full[TC_STAGES];       // 128 producer arrivals (A hi / lo stored)
+  uint64_t bfull[TC_STAGES];      // 1 arrival + 32 KB of B bulk copies
+  uint64_t empty[TC_STAGES];      // tcgen05.commit after the stage's MMAs
+  uint64_t acc_full[2];           // tcgen05.commit after a tile's last K block
+  uint64_t acc_empty[2];          // 128 epilogue arrivals
+  uint32_t tmem;
+  int failed;
+};
+
+// Row geometry of tile row `row` of global tile `tile`: problem index, A row pointer (null when out of range),
+// output row pointer and scale.
+struct TcRow {
+  int pi;
+  int nk;
+  const float* a;
+  float* y;
+  float alpha;
+};
+
+__device__ __forceinline__ TcRow tc_row(const GemmGroup& grp, int tile, int row) {
+  TcRow o;
+  o.pi = gemm_problem_of(grp, tile);
+  const GemmProblem& g = grp.p[o.pi];
+  o.nk = g.nseg * (MB_C / TC_BK);
+  o.a = nullptr;
+  o.y = nullptr;
+  o.alpha = 1.f;
+  const int64_t r = (int64_t)(tile - grp.tile_start[o.pi]) * TC_BM + row;
+  if (r < (int64_t)g.n_atoms * g.mult) {
+    const int64_t t = r / g.mult;
+    const int mm = (int)(r - t * g.mult);
+    const int64_t at = g.order ? g.order[t] : t;
+    o.a = g.X + at * g.ldx + (int64_t)mm * MB_C;
+    o.y = g.Y + at * g.ldy + (int64_t)(g.yoff + mm) * MB_C;
+    if (g.rho) o.alpha = 1.f / (g.rho[at] + 1.f);
+  }
+  return o;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ GemmGroup grp, int n_tiles) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);   // [2] stage barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + TC_STAGES);
-  __shared__ int s_failed;
-  const int pi = gemm_problem_of(grp, blockIdx.x);
-  const GemmProblem& g = grp.p[pi];
+  TcBars& B = *reinterpret_cast<TcBars*>(smem + TC_BAR_OFF);
+  volatile int* failed = &B.failed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t nrows = (int64_t)g.n_atoms * g.mult;
-  const int64_t r0 = (int64_t)(blockIdx.x - grp.tile_start[pi]) * TC_BM;
 
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TC_BN)
+  if (warp == TC_MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem)),
+                 "r"(TC_ACC_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  if (tid == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) mbar_init(&bar[s], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_failed = 0;
+    if (lane == 0) {
+      for (int s = 0; s < TC_STAGES; ++s) {
+        mbar_init(&B.full[s], 128);
+        mbar_init(&B.bfull[s], 1);
+        mbar_init(&B.empty[s], 1);
+      }
+      for (int a = 0; a < 2; ++a) {
+        mbar_init(&B.acc_full[a], 1);
+        mbar_init(&B.acc_empty[a], 128);
+      }
+      B.failed = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = B.tmem;
 
-  // A row owned by this thread (two threads per row, 16 floats = 4 chunks each of the 32-float K block)
-  const int arow_i = tid >> 1, ahalf = tid & 1;
-  const float* arow = nullptr;
-  {
-    const int64_t r = r0 + arow_i;
-    if (r < nrows) {
-      const int64_t t = r / g.mult;
-      const int mm = (int)(r - t * g.mult);
-      const int64_t at = g.order ? g.order[t] : t;
-      arow = g.X + at * g.ldx + (int64_t)mm * MB_C;
-    }
-  }
-  const int nK = g.nseg * (MB_C / TC_BK);
-  const uint32_t idesc = tf32_idesc(TC_BM, TC_BN);
-  // register prefetch of one K block: A (4 float4 of this thread's row half), B hi / lo (4 float4 each)
-  float4 ra[4], rbh[4], rbl[4];
-  auto load_block = [&](int kb) {
-    const int seg = (kb * TC_BK) / MB_C, kin = kb * TC_BK - seg * MB_C;
+  if (warp < 4) {
+    // ------------------------------------------------------------------------------------------ producers
+    const int p = tid;
+    unsigned char* raw = smem + TC_RAW_OFF;
+    // issue cursor (tile, kb) running TC_RAW blocks ahead of the split cursor; the next tile's row geometry is
+    // computed one tile early so its dependent loads (order, rho) are off the critical path
+    int it_tile = blockIdx.x, it_kb = 0;
+    TcRow it_rw = tc_row(grp, it_tile, p);
+    TcRow it_next = it_tile + (int)gridDim.x < n_tiles ? tc_row(grp, it_tile + gridDim.x, p) : it_rw;
+    auto issue_next = [&](int slot) {
+      if (it_tile < n_tiles) {
+        if (it_rw.a) {
+          const GemmProblem& g = grp.p[it_rw.pi];
+          const int seg = (it_kb * TC_BK) / MB_C, kin = it_kb * TC_BK - seg * MB_C;
+          const float* src = it_rw.a + (int64_t)g.xoff[seg] * MB_C + kin;
+          unsigned char* dst = raw + slot * TC_RAW_BYTES + p * TC_RAW_ROW;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      ra[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (arow) ra[q] = *reinterpret_cast<const float4*>(arow + (int64_t)g.xoff[seg] * MB_C + kin + (ahalf * 4 + q) * 4);
-    }
-    const float* bseg = g.B + (int64_t)seg * MB_C * MB_C + kin;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int idx = tid + q * TC_THREADS;          // 0 .. 1023 over (n, chunk)
-      const float* src = bseg + (int64_t)(idx >> 3) * MB_C + (idx & 7) * 4;
-      rbh[q] = __ldg(reinterpret_cast<const float4*>(src));
-      rbl[q] = __ldg(reinterpret_cast<const float4*>(src + g.plane));
-    }
-  };
-  load_block(0);
-  bool ok = true;
-  for (int kb = 0; kb < nK; ++kb) {
-    const int s = kb & 1;
-    if (kb >= TC_STAGES) {
-      if (!mbar_wait(&bar[s], (uint32_t)(((kb - TC_STAGES) / TC_STAGES) & 1))) ok = false;
-    }
-    unsigned char* st = smem + s * TC_STAGE_BYTES;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 v = ra[q];
-      float4 hi, lo;
-      hi.x = tf32_rna(v.x); lo.x = tf32_rna(v.x - hi.x);
-      hi.y = tf32_rna(v.y); lo.y = tf32_rna(v.y - hi.y);
-      hi.z = tf32_rna(v.z); lo.z = tf32_rna(v.z - hi.z);
-      hi.w = tf32_rna(v.w); lo.w = tf32_rna(v.w - hi.w);
-      const uint32_t off = sw128_offset(arow_i, ahalf * 4 + q);
-      *reinterpret_cast<float4*>(st + off) = hi;
-      *reinterpret_cast<float4*>(st + TC_TILE_BYTES + off) = lo;
-      const int idx = tid + q * TC_THREADS;
-      const uint32_t boff = sw128_offset(idx >> 3, idx & 7);
-      *reinterpret_cast<float4*>(st + 2 * TC_TILE_BYTES + boff) = rbh[q];
-      *reinterpret_cast<float4*>(st + 3 * TC_TILE_BYTES + boff) = rbl[q];
-    }
-    if (kb + 1 < nK) load_block(kb + 1);             // in flight while this block is issued
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_hi = smem_u32(st), a_lo = a_hi + TC_TILE_BYTES;
-      const uint32_t b_hi = a_hi + 2 * TC_TILE_BYTES, b_lo = a_hi + 3 * TC_TILE_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < TC_BK / 8; ++kk) {
-        const uint32_t ko = kk * 32;                 // 8 tf32 = 32 bytes along K inside the swizzle atom
-        mma_tf32(tmem, sw128_desc(a_hi + ko), sw128_desc(b_hi + ko), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        mma_tf32(tmem, sw128_desc(a_hi + ko), sw128_desc(b_lo + ko), idesc, 1u);
-        mma_tf32(tmem, sw128_desc(a_lo + ko), sw128_desc(b_hi + ko), idesc, 1u);
-      }
-      mma_commit(&bar[s]);
-    }
-  }
-  // all MMAs done: the last commit covers every earlier tcgen05 op of the issuing thread
-  {
-    const int kl = nK - 1;
-    if (!mbar_wait(&bar[kl & 1], (uint32_t)((kl / TC_STAGES) & 1))) ok = false;
-  }
-  if (!ok) s_failed = 1;
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (s_failed) {
-    if (tid == 0) set_status(grp.status, MB_ST_TC_TIMEOUT);
-  } else {
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows), columns (w / 4) * 64 .. +63
-    const int lrow = (warp & 3) * 32 + lane;
-    const int col0 = (warp >> 2) * 64;
-    const int64_t r = r0 + lrow;
-    float v[64];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t x[32];
-      const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(col0 + 32 * h);
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-          "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-          : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
-            "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15]),
-            "=r"(x[16]), "=r"(x[17]), "=r"(x[18]), "=r"(x[19]), "=r"(x[20]), "=r"(x[21]), "=r"(x[22]), "=r"(x[23]),
-            "=r"(x[24]), "=r"(x[25]), "=r"(x[26]), "=r"(x[27]), "=r"(x[28]), "=r"(x[29]), "=r"(x[30]), "=r"(x[31])
-          : "r"(taddr));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[32 * h + j] = __uint_as_float(x[j]);
-    }
-    if (r < nrows) {
-      const int64_t t = r / g.mult;
-      const int mm = (int)(r - t * g.mult);
-      const int64_t at = g.order ? g.order[t] : t;
-      const float alpha = g.rho ? 1.f / (g.rho[at] + 1.f) : 1.f;
-      float* y = g.Y + at * g.ldy + (int64_t)(g.yoff + mm) * MB_C + col0;
-#pragma unroll
-      for (int j = 0; j < 64; j += 4) {
-        float4 o = make_float4(v[j] * alpha, v[j + 1] * alpha, v[j + 2] * alpha, v[j + 3] * alpha);
-        float4* yp = reinterpret_cast<float4*>(y + j);
-        if (g.accumulate) {
-          const float4 p = *yp;
-          o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+          for (int q = 0; q < 8; ++q) cp_async16(dst + 16 * q, src + 4 * q);
         }
-        *yp = o;
+        if (++it_kb == it_rw.nk) {
+          it_kb = 0;
+          it_tile += gridDim.x;
+          it_rw = it_next;
+          if (it_tile + (int)gridDim.x < n_tiles) it_next = tc_row(grp, it_tile + gridDim.x, p);
+        }
       }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+#pragma unroll 1
+    for (int q = 0; q < TC_RAW; ++q) issue_next(q);
+    int seq = 0;                                   // K blocks consumed (stage / phase counter)
+    TcRow rw = tc_row(grp, blockIdx.x, p);
+    for (int tile = blockIdx.x; tile < n_tiles && !*failed; tile += gridDim.x) {
+      const GemmProblem& g = grp.p[rw.pi];
+      const int nk = rw.nk;
+      const bool have = rw.a != nullptr;
+      for (int kb = 0; kb < nk; ++kb, ++seq) {
+        const int s = seq % TC_STAGES, slot = seq % TC_RAW;
+        asm volatile("cp.async.wait_group %0;" ::"n"(TC_RAW - 1) : "memory");
+        float4 v[8];
+        const unsigned char* src = raw + slot * TC_RAW_BYTES + p * TC_RAW_ROW;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          v[q] = have ? *reinterpret_cast<const float4*>(src + 16 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        issue_next(slot);                          // the slot has been read: refill it TC_RAW blocks ahead
+        // stage s free once the MMAs of its previous use completed (first use: the preceding phase counts done)
+        if (!mbar_wait(&B.empty[s], ((seq / TC_STAGES) & 1) ^ 1)) {
+          *failed = 1;
+          break;
+        }
+        unsigned char* st = smem + s * TC_STAGE_BYTES;
+        if (p == 0) {
+          const int seg = (kb * TC_BK) / MB_C, kin = kb * TC_BK - seg * MB_C;
+          const float* bsrc = g.B + (int64_t)seg * MB_C * MB_C + (int64_t)(kin / TC_BK) * (TC_BM * TC_BK);
+          mbar_arrive_tx(&B.bfull[s], 2 * TC_TILE_BYTES);
+          bulk_g2s(st + 2 * TC_TILE_BYTES, bsrc, TC_TILE_BYTES, &B.bfull[s]);
+          bulk_g2s(st + 3 * TC_TILE_BYTES, bsrc + g.plane, TC_TILE_BYTES, &B.bfull[s]);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 hi, lo;
+          hi.x = tf32_rna(v[q].x); lo.x = tf32_rna(v[q].x - hi.x);
+          hi.y = tf32_rna(v[q].y); lo.y = tf32_rna(v[q].y - hi.y);
+          hi.z = tf32_rna(v[q].z); lo.z = tf32_rna(v[q].z - hi.z);
+          hi.w = tf32_rna(v[q].w); lo.w = tf32_rna(v[q].w - hi.w);
+          const uint32_t off = sw128_offset(p, q);
+          *reinterpret_cast<float4*>(st + off) = hi;
+          *reinterpret_cast<float4*>(st + TC_TILE_BYTES + off) = lo;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&B.full[s]);
+      }
+      if (tile + (int)gridDim.x < n_tiles) rw = tc_row(grp, tile + gridDim.x, p);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    // after a timeout: B copies this thread issued may still be landing in the stages
+    if (p == 0 && *failed)
+      for (int s = 0; s < TC_STAGES; ++s) {
+        const int last = seq - 1 - ((seq - 1 - s) % TC_STAGES + TC_STAGES) % TC_STAGES;   // last seq using stage s
+        if (last >= 0) mbar_wait(&B.bfull[s], (last / TC_STAGES) & 1);
+      }
+  } else if (warp < TC_MMA_WARP) {
+    // ------------------------------------------------------------------------------------------ epilogue
+    const int q4 = warp & 3, row = q4 * 32 + lane;
+    int tc = 0;
+    // every exit decision is warp-uniform: the loop body holds warp-collective tcgen05.ld.sync.aligned
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tc) {
+      if (__shfl_sync(0xffffffffu, *failed, 0)) break;
+      const int a = tc & 1;
+      const TcRow rw = tc_row(grp, tile, row);     // its loads overlap the wait
+      if (!__all_sync(0xffffffffu, mbar_wait(&B.acc_full[a], (tc >> 1) & 1))) {
+        *failed = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int acc = grp.p[rw.pi].accumulate;
+      float* stg = reinterpret_cast<float*>(smem + TC_EPI_OFF) + q4 * 32 * TC_EPI_ROW;   // this warp's chunk
+      // lane l stores rows 4 i + l / 8 (i = 0..7), columns 4 (l % 8) .. + 3 of the chunk: 4 rows per instruction
+      const int srow = lane >> 3, scol = (lane & 7) * 4;
+#pragma unroll 1
+      for (int h = 0; h < 4; ++h) {
+        uint32_t x[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(a * TC_BN + 32 * h);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+            "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+            : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
+              "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15]),
+              "=r"(x[16]), "=r"(x[17]), "=r"(x[18]), "=r"(x[19]), "=r"(x[20]), "=r"(x[21]), "=r"(x[22]), "=r"(x[23]),
+              "=r"(x[24]), "=r"(x[25]), "=r"(x[26]), "=r"(x[27]), "=r"(x[28]), "=r"(x[29]), "=r"(x[30]), "=r"(x[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        __syncwarp();                                // the previous chunk's reads of the staging area are done
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stg[lane * TC_EPI_ROW + j] = __uint_as_float(x[j]) * rw.alpha;
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + srow;                // row of this warp's 32 (lane r of the TMEM load)
+          float* yrow = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(rw.y), r));
+          if (yrow) {
+            const float* sv = stg + r * TC_EPI_ROW + scol;
+            float4 o = make_float4(sv[0], sv[1], sv[2], sv[3]);
+            float4* yp = reinterpret_cast<float4*>(yrow + 32 * h + scol);
+            if (acc) {
+              const float4 p4 = *yp;
+              o.x += p4.x; o.y += p4.y; o.z += p4.z; o.w += p4.w;
+            }
+            *yp = o;
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&B.acc_empty[a]);
+    }
+  } else if (lane == 0) {
+    // ------------------------------------------------------------------------------------------ MMA issue
+    const uint32_t idesc = tf32_idesc(TC_BM, TC_BN);
+    int seq = 0, tc = 0;
+    uint64_t* last_bar = nullptr;
+    uint32_t last_par = 0;
+    for (int tile = blockIdx.x; tile < n_tiles && !*failed; tile += gridDim.x, ++tc) {
+      const int a = tc & 1;
+      if (!mbar_wait(&B.acc_empty[a], ((tc >> 1) & 1) ^ 1)) {
+        *failed = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int nk = grp.p[gemm_problem_of(grp, tile)].nseg * (MB_C / TC_BK);
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb, ++seq) {
+        const int s = seq % TC_STAGES;
+        const uint32_t ph = (seq / TC_STAGES) & 1;
+        if (!mbar_wait(&B.full[s], ph) || !mbar_wait(&B.bfull[s], ph)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = smem_u32(smem + s * TC_STAGE_BYTES), a_lo = a_hi + TC_TILE_BYTES;
+        const uint32_t b_hi = a_hi + 2 * TC_TILE_BYTES, b_lo = a_hi + 3 * TC_TILE_BYTES;
+        const uint32_t d = tmem + (uint32_t)(a * TC_BN);
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 8; ++kk) {
+          const uint32_t ko = kk * 32;               // 8 tf32 = 32 bytes along K inside the swizzle atom
+          mma_tf32(d, sw128_desc(a_hi + ko), sw128_desc(b_hi + ko), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32(d, sw128_desc(a_hi + ko), sw128_desc(b_lo + ko), idesc, 1u);
+          mma_tf32(d, sw128_desc(a_lo + ko), sw128_desc(b_hi + ko), idesc, 1u);
+        }
+        mma_commit(&B.empty[s]);
+        last_bar = &B.empty[s];
+        last_par = ph;
+      }
+      if (!ok) {
+        *failed = 1;
+        break;
+      }
+      mma_commit(&B.acc_full[a]);
+      last_bar = &B.acc_full[a];
+      last_par = (tc >> 1) & 1;
+    }
+    // after a timeout: wait (bounded) for the MMAs already issued before the TMEM is freed
+    if (*failed && last_bar) mbar_wait(last_bar, last_par);
   }
+  if (tid == 0 && *failed) set_status(grp.status, MB_ST_TC_TIMEOUT);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) {
+  if (warp == TC_MMA_WARP) {
+    __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_ACC_COLS) : "memory");
   }
 }
 
-static bool g_tc_attr_set = false;
+static int g_tc_attr_dev = -1;
+static int g_tc_sms = 0;
 
 int gemm_group_launch_tc(const GemmGroup& grp0, cudaStream_t st) {
-  if (!g_tc_attr_set) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("node_gemm_tc (device)");
+  if (g_tc_attr_dev != dev) {
     if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess) {
       set_error("node_gemm_tc: cannot reserve %d bytes of shared memory", TC_SMEM);
       return MB_E_CUDA;
     }
-    g_tc_attr_set = true;
+    if (cudaDeviceGetAttribute(&g_tc_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_tc_sms < 1) {
+      set_error("node_gemm_tc: cannot query the SM count");
+      return MB_E_CUDA;
+    }
+    g_tc_attr_dev = dev;
   }
   GemmGroup grp = grp0;
   int tiles = 0;
   for (int q = 0; q < grp.n; ++q) {
+    const GemmProblem& p = grp.p[q];
+    if ((reinterpret_cast<uintptr_t>(p.X) | reinterpret_cast<uintptr_t>(p.Y) | reinterpret_cast<uintptr_t>(p.B)) & 15 ||
+        (p.plane % 4)) {
+      set_error("node_gemm_tc: X, Y and B must be 16-byte aligned (and the plane stride a multiple of 4)");
+      return MB_E_ARG;
+    }
     grp.tile_start[q] = tiles;
-    tiles += (int)(((int64_t)grp.p[q].n_atoms * grp.p[q].mult + TC_BM - 1) / TC_BM);
+    tiles += (int)(((int64_t)p.n_atoms * p.mult + TC_BM - 1) / TC_BM);
   }
   grp.tile_start[grp.n] = tiles;
   if (tiles == 0) return 0;
-  k_gemm_tc<<<tiles, TC_THREADS, TC_SMEM, st>>>(grp);
+  const int grid = tiles < g_tc_sms ? tiles : g_tc_sms;
+  k_gemm_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(grp, tiles);
   return check_launch("node_gemm_tc");
 }
 

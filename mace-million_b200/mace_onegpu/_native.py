@@ -119,7 +119,7 @@ def byref(s):
     return ctypes.byref(s)
 
 
-KINDS = ("edge_l1_fwd", "edge_l1_bwd", "edge_l2_fwd", "edge_l2_bwd", "symcon")
+KINDS = ("edge_l1_fwd", "edge_l1_bwd", "edge_l2_fwd", "edge_l2_bwd", "symcon", "node_gemm")
 
 
 def timing(enable: bool):

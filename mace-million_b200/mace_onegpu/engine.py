@@ -48,6 +48,30 @@ def tc_split(B: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(np.stack([hi, lo]))
 
 
+def sw128_positions() -> np.ndarray:
+    """Position of element (n, k) of a 128 x 128 K-major tile set in its shared-memory image: four K blocks of 32
+    (16 KB each), each in the SWIZZLE_128B layout that tcgen05 descriptors read (8-row groups of 1024 B, row n at
+    (n % 8) * 128 B, 16-byte chunk c of the row at chunk position c ^ (n % 8)).  Flat [n * 128 + k] -> float index."""
+    n = np.arange(128)[:, None]
+    k = np.arange(128)[None, :]
+    c = (k % 32) // 4
+    pos = (k // 32) * 4096 + (n // 8) * 256 + (n % 8) * 32 + (c ^ (n % 8)) * 4 + k % 4
+    return pos.ravel()
+
+
+def tc_planes(B: np.ndarray) -> np.ndarray:
+    """GEMM B operands for the tcgen05 kernel: tf32 hi / lo planes (tc_split) with every 128 x 128 matrix permuted
+    into its SWIZZLE_128B K-block image, so the kernel stages each 16 KB K block with one bulk copy.  Same shape,
+    element count and matrix offsets as tc_split."""
+    planes = tc_split(B)
+    if planes.shape[-2:] != (128, 128):
+        raise ValueError("tcgen05 GEMM operands are 128 x 128 matrices")
+    flat = planes.reshape(-1, 128 * 128)
+    out = np.empty_like(flat)
+    out[:, sw128_positions()] = flat
+    return out.reshape(planes.shape)
+
+
 def fold_weights(model: Mdl.MACEModel, cols) -> dict:
     """All folded fp64 arrays (CPU numpy) for the species columns `cols` (model one-hot columns present)."""
     a = model.arch
@@ -153,8 +177,8 @@ class FoldedModel:
         for name, key, transpose in (("M0", "M0", False), ("Wp1", "Wp1", False), ("Wup2", "Wup2", False),
                                      ("Wsk1", "Wsk1", False), ("Wlin2", "Wlin2", False), ("Wp2", "Wp2", False)):
             W = f[key]
-            t[name + "_tc"] = torch.as_tensor(tc_split(W), device=dev).contiguous()
-            t[name + "T_tc"] = torch.as_tensor(tc_split(np.swapaxes(W, -1, -2)), device=dev).contiguous()
+            t[name + "_tc"] = torch.as_tensor(tc_planes(W), device=dev).contiguous()
+            t[name + "T_tc"] = torch.as_tensor(tc_planes(np.swapaxes(W, -1, -2)), device=dev).contiguous()
         # spline tables built on the GPU in fp64 (tab1 carries X1 of the sender species)
         self.TV, self.TG = {}, {}
         for i, key, D, csk in ((0, "tab1", 4 * C, "col_scale1"), (1, "tab2", 10 * C, None)):

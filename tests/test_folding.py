@@ -118,3 +118,16 @@ def test_sc_layout_fingerprint_stable():
         ents = o3.sc_entries(Ls)
         assert o3.sc_fingerprint(ents) == o3.sc_fingerprint(o3.sc_entries(Ls))
     assert len(o3.sc_entries((0, 1))) == 410 and len(o3.sc_entries((0,))) == 94
+
+
+def test_tc_planes_are_the_swizzled_split():
+    """The tcgen05 B operand image: a permutation of each 128 x 128 matrix of the tf32 hi / lo split."""
+    rng = np.random.default_rng(3)
+    B = rng.normal(size=(3, 128, 128))
+    pos = E.sw128_positions()
+    assert sorted(pos.tolist()) == list(range(128 * 128))
+    planes = E.tc_planes(B)
+    split = E.tc_split(B)
+    assert planes.shape == split.shape
+    back = planes.reshape(-1, 128 * 128)[:, pos].reshape(split.shape)
+    assert np.array_equal(back, split)

@@ -17,7 +17,7 @@ def _run(tc, X, ldx, xoff, B, Y, ldy, yoff, mult, order, n, rho, acc):
     st = torch.cuda.current_stream().cuda_stream
     xo = (N.c_i32 * 4)(*(list(xoff) + [0] * (4 - len(xoff))))
     if tc:
-        Bt = torch.as_tensor(E.tc_split(B.double().cpu().numpy()), device="cuda").contiguous()
+        Bt = torch.as_tensor(E.tc_planes(B.double().cpu().numpy()), device="cuda").contiguous()
         status = torch.zeros(1, dtype=torch.int32, device="cuda")
         N.check(L.mace_b200_node_gemm_tc(N.ptr(X), ldx, xo, len(xoff), N.ptr(Bt), Bt[0].numel(), N.ptr(Y), ldy, yoff,
                                          mult, N.ptr(order), n, N.ptr(rho), acc, N.ptr(status), st), "gemm_tc")
@@ -35,6 +35,9 @@ def _run(tc, X, ldx, xoff, B, Y, ldy, yoff, mult, order, n, rho, acc):
     (5, [4], 16, 4, 16, 129, True, True, 0),
     (7, [26, 33], 40, 9, 16, 517, False, True, 0),
     (3, [2, 5, 8], 40, 1, 16, 2048, False, True, 1),
+    # more tiles than SMs: every persistent CTA runs several tiles, both TMEM accumulators and all stage phases wrap
+    (3, [1], 4, 1, 4, 50000, True, True, 1),
+    (1, [0, 2], 4, 1, 4, 70001, False, False, 0),
 ])
 def test_tc_gemm_matches_simt(mult, xoff, ncomp, yoff, ycomp, n, use_order, use_rho, acc):
     g = torch.Generator(device="cuda").manual_seed(1)
