@@ -247,6 +247,30 @@ int mace_b200_finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* 
 int mace_b200_pack_rows(const float* src, const int32_t* idx, int64_t n, int32_t D, float* buf, void* stream);
 int mace_b200_unpack_add_rows(const float* buf, const int32_t* idx, int64_t n, int32_t D, float* dst, void* stream);
 
+/* ---------------------------------------------------------------- neighbour lists (input preparation)
+ * Replaces System.build_neighbors (mace_onegpu/receiver_chunk_mace.py:114-165) for the standalone driver: full
+ * lists (both directions) of receivers [0, n_recv) within r_cut, one warp per receiver over the 27 candidate cells.
+ * Cells: lo[3], width[3] (>= r_cut), nc[3]; cell of x = clamp(floor((x - lo) / width)), linear index
+ * (cx * nc1 + cy) * nc2 + cz; cell_start [ncell + 1] and cell_atoms (atom indices grouped by cell) are the caller's.
+ * periodic = 1: orthorhombic box[3], minimum image, positions wrapped into [0, box), nc >= 3 per dimension;
+ * periodic = 0: no wrap (explicit ghost atoms; all atoms, receivers first, are in the cells).
+ * Output order: by receiver, candidates in a fixed order (deterministic); rij = x_i - x_j (fp64).
+ * nbr_count writes counts [n_recv]; the caller forms rowptr [n_recv + 1] (int64 prefix sum) and calls nbr_fill.
+ * verlet_filter: pairs vrow / vj of a skin list kept when |x_i - x_j| < r_cut at the current positions; with
+ * counts != null it counts, else it fills (pi, pj, rij) at rowptr.  A count / fill mismatch sets
+ * MB_ST_BAD_ROWPTR in *status (may be null). */
+int mace_b200_nbr_count(const double* pos, const int32_t* cell_start, const int32_t* cell_atoms, const double* lo,
+                        const double* width, const int32_t* nc, const double* box, int32_t periodic, int32_t n_recv,
+                        double r_cut, int32_t* counts, void* stream);
+int mace_b200_nbr_fill(const double* pos, const int32_t* cell_start, const int32_t* cell_atoms, const double* lo,
+                       const double* width, const int32_t* nc, const double* box, int32_t periodic, int32_t n_recv,
+                       double r_cut, const int64_t* rowptr, int32_t* pi, int32_t* pj, double* rij, uint32_t* status,
+                       void* stream);
+int mace_b200_verlet_filter(const double* pos, const double* box, int32_t periodic, int32_t n_recv,
+                            const int64_t* vrow, const int32_t* vj, double r_cut, int32_t* counts,
+                            const int64_t* rowptr, int32_t* pi, int32_t* pj, double* rij, uint32_t* status,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,234 @@
+// Full neighbour lists on the GPU (input preparation of the standalone driver and of the multi-GPU ghosts; the force
+// evaluation itself takes the pair list as given, like the ML-IAP boundary).  Cell list with cells of at least
+// r_cut, 27 candidate cells per atom, the algorithm of the reference's System.build_neighbors
+// (mace_onegpu/receiver_chunk_mace.py:114-165): a count pass and a fill pass over the same candidates, one warp per
+// receiver.  Candidates are visited in a fixed order (cell offsets dx, dy, dz = -1..1 nested, atoms of a cell in the
+// caller's cell-sorted order), hits are compacted with ballots, so the output is deterministic.
+//
+// Periodic mode: orthorhombic box, minimum image, at least 3 cells per dimension (no candidate is seen twice).
+// Open mode: cells over the caller's bounding box, no wrap (explicit ghost images).
+// The Verlet filter keeps, per receiver, the pairs of a skin list that are within r_cut at the current positions.
+#include "common.cuh"
+
+namespace mb {
+
+struct CellGrid {
+  double lo[3], inv_w[3], box[3];
+  int nc[3];
+  int periodic;
+};
+
+__device__ __forceinline__ int cell_coord(double x, double lo, double inv_w, int nc) {
+  int c = (int)floor((x - lo) * inv_w);
+  return c < 0 ? 0 : (c >= nc ? nc - 1 : c);
+}
+
+__device__ __forceinline__ void min_image(double& d, double box, int periodic) {
+  if (periodic) d -= box * rint(d / box);
+}
+
+// Visits the candidates of receiver i (one warp); fn(k_first_of_pass, hit_mask, j, dx, dy, dz) per 32-wide step.
+template <typename Fn>
+__device__ __forceinline__ void for_candidates(const double* __restrict__ pos, const int* __restrict__ cell_start,
+                                               const int* __restrict__ cell_atoms, const CellGrid& g, int i, double r2,
+                                               Fn fn) {
+  const int lane = threadIdx.x & 31;
+  const double xi = pos[3 * (int64_t)i], yi = pos[3 * (int64_t)i + 1], zi = pos[3 * (int64_t)i + 2];
+  const int ci[3] = {cell_coord(xi, g.lo[0], g.inv_w[0], g.nc[0]), cell_coord(yi, g.lo[1], g.inv_w[1], g.nc[1]),
+                     cell_coord(zi, g.lo[2], g.inv_w[2], g.nc[2])};
+  for (int ox = -1; ox <= 1; ++ox)
+    for (int oy = -1; oy <= 1; ++oy)
+      for (int oz = -1; oz <= 1; ++oz) {
+        int c3[3] = {ci[0] + ox, ci[1] + oy, ci[2] + oz};
+        bool ok = true;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          if (c3[d] < 0 || c3[d] >= g.nc[d]) {
+            if (!g.periodic) ok = false;
+            c3[d] = (c3[d] + g.nc[d]) % g.nc[d];
+          }
+        }
+        if (!ok) continue;
+        const int c = (c3[0] * g.nc[1] + c3[1]) * g.nc[2] + c3[2];
+        const int s = cell_start[c], e = cell_start[c + 1];
+        for (int k0 = s; k0 < e; k0 += 32) {
+          const int k = k0 + lane;
+          int j = -1;
+          double dx = 0.0, dy = 0.0, dz = 0.0;
+          bool hit = false;
+          if (k < e) {
+            j = cell_atoms[k];
+            dx = xi - pos[3 * (int64_t)j];
+            dy = yi - pos[3 * (int64_t)j + 1];
+            dz = zi - pos[3 * (int64_t)j + 2];
+            min_image(dx, g.box[0], g.periodic);
+            min_image(dy, g.box[1], g.periodic);
+            min_image(dz, g.box[2], g.periodic);
+            hit = j != i && dx * dx + dy * dy + dz * dz < r2;
+          }
+          fn(__ballot_sync(0xffffffffu, hit), hit, j, dx, dy, dz);
+        }
+      }
+}
+
+__global__ void k_nbr_count(const double* __restrict__ pos, const int* __restrict__ cell_start,
+                            const int* __restrict__ cell_atoms, const CellGrid g, int n_recv, double r2,
+                            int* __restrict__ counts) {
+  const int i = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (i >= n_recv) return;
+  int cnt = 0;
+  for_candidates(pos, cell_start, cell_atoms, g, i, r2,
+                 [&](unsigned mask, bool, int, double, double, double) { cnt += __popc(mask); });
+  if ((threadIdx.x & 31) == 0) counts[i] = cnt;
+}
+
+__global__ void k_nbr_fill(const double* __restrict__ pos, const int* __restrict__ cell_start,
+                           const int* __restrict__ cell_atoms, const CellGrid g, int n_recv, double r2,
+                           const int64_t* __restrict__ rowptr, int* __restrict__ pi, int* __restrict__ pj,
+                           double* __restrict__ rij, unsigned* __restrict__ status) {
+  const int i = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (i >= n_recv) return;
+  const int lane = threadIdx.x & 31;
+  int64_t o = rowptr[i];
+  const int64_t end = rowptr[i + 1];
+  for_candidates(pos, cell_start, cell_atoms, g, i, r2,
+                 [&](unsigned mask, bool hit, int j, double dx, double dy, double dz) {
+                   if (hit) {
+                     const int64_t q = o + __popc(mask & ((1u << lane) - 1u));
+                     if (q < end) {
+                       pi[q] = i;
+                       pj[q] = j;
+                       rij[3 * q] = dx;
+                       rij[3 * q + 1] = dy;
+                       rij[3 * q + 2] = dz;
+                     }
+                   }
+                   o += __popc(mask);
+                 });
+  if (lane == 0 && o != end) set_status(status, ST_BAD_ROWPTR);   // positions changed between count and fill
+}
+
+// Verlet filter: pairs [vrow[i], vrow[i+1]) of receiver i (senders vj) that are within r_cut now.
+template <bool FILL>
+__global__ void k_verlet_filter(const double* __restrict__ pos, const CellGrid g, int n_recv,
+                                const int64_t* __restrict__ vrow, const int* __restrict__ vj, double r2,
+                                int* __restrict__ counts, const int64_t* __restrict__ rowptr, int* __restrict__ pi,
+                                int* __restrict__ pj, double* __restrict__ rij, unsigned* __restrict__ status) {
+  const int i = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (i >= n_recv) return;
+  const int lane = threadIdx.x & 31;
+  const double xi = pos[3 * (int64_t)i], yi = pos[3 * (int64_t)i + 1], zi = pos[3 * (int64_t)i + 2];
+  const int64_t s = vrow[i], e = vrow[i + 1];
+  int64_t o = FILL ? rowptr[i] : 0;
+  for (int64_t k0 = s; k0 < e; k0 += 32) {
+    const int64_t k = k0 + lane;
+    bool hit = false;
+    int j = -1;
+    double dx = 0.0, dy = 0.0, dz = 0.0;
+    if (k < e) {
+      j = vj[k];
+      dx = xi - pos[3 * (int64_t)j];
+      dy = yi - pos[3 * (int64_t)j + 1];
+      dz = zi - pos[3 * (int64_t)j + 2];
+      min_image(dx, g.box[0], g.periodic);
+      min_image(dy, g.box[1], g.periodic);
+      min_image(dz, g.box[2], g.periodic);
+      hit = dx * dx + dy * dy + dz * dz < r2;
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, hit);
+    if (FILL && hit) {
+      const int64_t q = o + __popc(mask & ((1u << lane) - 1u));
+      if (q < rowptr[i + 1]) {
+        pi[q] = i;
+        pj[q] = j;
+        rij[3 * q] = dx;
+        rij[3 * q + 1] = dy;
+        rij[3 * q + 2] = dz;
+      }
+    }
+    o += __popc(mask);
+  }
+  if (lane == 0) {
+    if (!FILL)
+      counts[i] = (int)o;
+    else if (o != rowptr[i + 1])
+      set_status(status, ST_BAD_ROWPTR);
+  }
+}
+
+static int make_grid(const double* lo, const double* width, const int32_t* nc, const double* box, int periodic,
+                     CellGrid& g, const char* who) {
+  for (int d = 0; d < 3; ++d) {
+    if (nc[d] < 1 || !(width[d] > 0.0) || (periodic && (nc[d] < 3 || !(box[d] > 0.0)))) {
+      set_error("%s: bad cell grid (dimension %d: %d cells of %g; periodic boxes need >= 3 cells)", who, d, nc[d],
+                width[d]);
+      return MB_E_ARG;
+    }
+    g.lo[d] = lo[d];
+    g.inv_w[d] = 1.0 / width[d];
+    g.nc[d] = nc[d];
+    g.box[d] = periodic ? box[d] : 0.0;
+  }
+  g.periodic = periodic ? 1 : 0;
+  return 0;
+}
+
+static inline unsigned warp_blocks(int n) { return (unsigned)(((int64_t)n * 32 + 255) / 256); }
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int mace_b200_nbr_count(const double* pos, const int32_t* cell_start, const int32_t* cell_atoms,
+                                   const double* lo, const double* width, const int32_t* nc, const double* box,
+                                   int32_t periodic, int32_t n_recv, double r_cut, int32_t* counts, void* stream) {
+  CellGrid g;
+  if (int rc = make_grid(lo, width, nc, box, periodic, g, "nbr_count")) return rc;
+  if (!pos || !cell_start || !cell_atoms || !counts || n_recv < 0) {
+    set_error("nbr_count: null pointer or negative size");
+    return MB_E_ARG;
+  }
+  if (n_recv == 0) return 0;
+  k_nbr_count<<<warp_blocks(n_recv), 256, 0, (cudaStream_t)stream>>>(pos, cell_start, cell_atoms, g, n_recv,
+                                                                      r_cut * r_cut, counts);
+  return check_launch("nbr_count");
+}
+
+extern "C" int mace_b200_nbr_fill(const double* pos, const int32_t* cell_start, const int32_t* cell_atoms,
+                                  const double* lo, const double* width, const int32_t* nc, const double* box,
+                                  int32_t periodic, int32_t n_recv, double r_cut, const int64_t* rowptr, int32_t* pi,
+                                  int32_t* pj, double* rij, uint32_t* status, void* stream) {
+  CellGrid g;
+  if (int rc = make_grid(lo, width, nc, box, periodic, g, "nbr_fill")) return rc;
+  if (!pos || !cell_start || !cell_atoms || !rowptr || !pi || !pj || !rij || n_recv < 0) {
+    set_error("nbr_fill: null pointer or negative size");
+    return MB_E_ARG;
+  }
+  if (n_recv == 0) return 0;
+  k_nbr_fill<<<warp_blocks(n_recv), 256, 0, (cudaStream_t)stream>>>(pos, cell_start, cell_atoms, g, n_recv,
+                                                                     r_cut * r_cut, rowptr, pi, pj, rij, status);
+  return check_launch("nbr_fill");
+}
+
+extern "C" int mace_b200_verlet_filter(const double* pos, const double* box, int32_t periodic, int32_t n_recv,
+                                       const int64_t* vrow, const int32_t* vj, double r_cut, int32_t* counts,
+                                       const int64_t* rowptr, int32_t* pi, int32_t* pj, double* rij,
+                                       uint32_t* status, void* stream) {
+  if (!pos || !vrow || !vj || n_recv < 0 || (periodic && !box) || (!counts && !(rowptr && pi && pj && rij))) {
+    set_error("verlet_filter: null pointer or negative size");
+    return MB_E_ARG;
+  }
+  CellGrid g{};
+  g.periodic = periodic ? 1 : 0;
+  for (int d = 0; d < 3; ++d) g.box[d] = periodic ? box[d] : 0.0;
+  if (n_recv == 0) return 0;
+  const double r2 = r_cut * r_cut;
+  if (counts)
+    k_verlet_filter<false><<<warp_blocks(n_recv), 256, 0, (cudaStream_t)stream>>>(pos, g, n_recv, vrow, vj, r2, counts,
+                                                                                  nullptr, nullptr, nullptr, nullptr,
+                                                                                  status);
+  else
+    k_verlet_filter<true><<<warp_blocks(n_recv), 256, 0, (cudaStream_t)stream>>>(pos, g, n_recv, vrow, vj, r2, nullptr,
+                                                                                 rowptr, pi, pj, rij, status);
+  return check_launch("verlet_filter");
+}

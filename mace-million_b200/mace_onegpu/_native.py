@@ -71,6 +71,11 @@ _SIGS = {
     "mace_b200_finalize": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mace_b200_pack_rows": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp]),
     "mace_b200_unpack_add_rows": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp]),
+    "mace_b200_nbr_count": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_f64, c_vp, c_vp]),
+    "mace_b200_nbr_fill": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_f64, c_vp, c_vp, c_vp,
+                                   c_vp, c_vp, c_vp]),
+    "mace_b200_verlet_filter": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_f64, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                        c_vp, c_vp]),
 }
 
 _lib = None

@@ -1,9 +1,9 @@
 """Standalone velocity-Verlet molecular dynamics on one GPU with the B200 three-pass force evaluation (the MD run of
 dt = 1 fs, Verlet skin 2 A, Maxwell-Boltzmann velocities at 300 K), metal units (A, fs, eV, amu).
 
-The pair list is a Verlet list built at r_max + skin (cell list on the GPU, minimum image) and filtered to r < r_max
-every step, so the force call sees exactly the pairs LAMMPS' ML-IAP would hand over; it is rebuilt when any atom moved
-more than skin / 2 since the last build.  Forces F_i = -dE/dx_i come from the pair forces dE/drij with
+The pair list is a Verlet list built at r_max + skin (the library's cell-list kernels, minimum image) and filtered
+to r < r_max every step by the library's Verlet-filter kernels, so the force call sees exactly the pairs LAMMPS'
+ML-IAP would hand over; it is rebuilt when any atom moved more than skin / 2 since the last build.  Forces F_i = -dE/dx_i come from the pair forces dE/drij with
 rij = x_i - x_j: F_i -= PF, F_j += PF.
 
     python -m mace_onegpu.md --config water_1m --steps 100        (prints steps/s and ns/day)
@@ -44,17 +44,27 @@ class VelocityVerlet:
         self.F, self.epot = self._forces()
 
     def _build(self):
-        pi, pj, _ = NB.neighbor_list(self.x, self.box, self.r_max + self.skin, device=self.x.device)
-        self.vpi, self.vpj = pi.long(), pj.long()
+        self.x = torch.remainder(self.x, self.box)
+        pi, pj, _, vrow = NB.neighbor_list(self.x, self.box, self.r_max + self.skin, device=self.x.device,
+                                           return_rowptr=True)
+        self.vpi, self.vpj, self.vrow = pi, pj, vrow
         self.x_ref = self.x.clone()
         self.rebuilds += 1
 
-    def _forces(self):
-        d = self.x[self.vpi] - self.x[self.vpj]
+    def _pairs(self):
+        """Pairs within r_max at the current positions, from the Verlet list."""
+        if self.x.is_cuda:
+            return NB.verlet_filter(self.x, self.box, self.vrow, self.vpj, self.r_max)
+        vpi, vpj = self.vpi.long(), self.vpj.long()
+        d = self.x[vpi] - self.x[vpj]
         d = d - self.box * torch.round(d / self.box)
         keep = (d * d).sum(1) < self.r_max * self.r_max
-        pi, pj, rij = self.vpi[keep], self.vpj[keep], d[keep]
+        return self.vpi[keep], self.vpj[keep], d[keep]
+
+    def _forces(self):
+        pi, pj, rij = self._pairs()
         plan = self.eng.plan(pi, pj, rij, self.elems, self.n, self.n)
+        pi, pj = pi.long(), pj.long()
         eat, pf = self.eng.evaluate(plan)
         F = torch.zeros_like(self.x)
         F.index_add_(0, pi, -pf)
@@ -70,7 +80,6 @@ class VelocityVerlet:
         disp = self.x - self.x_ref
         disp = disp - self.box * torch.round(disp / self.box)
         if float((disp * disp).sum(1).max()) > (0.5 * self.skin) ** 2:
-            self.x = torch.remainder(self.x, self.box)
             self._build()
         self.F, self.epot = self._forces()
         self.v += 0.5 * self.dt * ACC * self.F / self.m
