@@ -27,6 +27,27 @@ __device__ __forceinline__ void set_status(unsigned* st, unsigned bit) {
   if (st) atomicOr(st, bit);
 }
 
+// ---------------------------------------------------------------------------------------------- spline rows
+// Spline-coefficient loads of the edge kernels: every edge streams its own (pair, interval) row from L2 once, so
+// the rows are read through the read-only path without allocating in L1 (MB_TAB_LOAD = 1, default), or with the
+// plain read-only load (0) or L2-only caching (2).
+#ifndef MB_TAB_LOAD
+#define MB_TAB_LOAD 1
+#endif
+__device__ __forceinline__ float4 tab_ld(const float4* p) {
+#if MB_TAB_LOAD == 1
+  float4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p));
+  return v;
+#elif MB_TAB_LOAD == 2
+  return __ldcg(p);
+#else
+  return __ldg(p);
+#endif
+}
+
 // ---------------------------------------------------------------------------------------------- reductions
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_fwd(const mb_model_t 
       for (int l = 0; l < 4; ++l) {
         float T[4];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) T[jj] = cubic(__ldg(rw + l * MB_C + 32 * jj), t);
+        for (int jj = 0; jj < 4; ++jj) T[jj] = cubic(tab_ld(rw + l * MB_C + 32 * jj), t);
 #pragma unroll
         for (int mm = l * l; mm < (l + 1) * (l + 1); ++mm)
 #pragma unroll
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1_BWD_MINB) k_edge_l1_bwd(c
         float T[4], G[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-          cq[jj] = __ldg(rw + l * MB_C + 32 * jj);
+          cq[jj] = tab_ld(rw + l * MB_C + 32 * jj);
           T[jj] = cubic(cq[jj], t);
         }
 #pragma unroll

@@ -120,62 +120,96 @@ int gemm_launch(const float* X, int64_t ldx, const int32_t* xoff, int nseg, cons
 }
 
 // ------------------------------------------------------------------------------------------------ symmetric contraction
-// One CTA per atom, one thread per channel.  x [n][16][C]; block 0 -> A [n][4][C], block 1 -> A [n][C].
-template <int BLK>
+// One thread per channel.  x [n][16][C]; block 0 -> A [n][4][C], block 1 -> A [n][C].  A CTA takes K atoms of one
+// species (consecutive entries of a species-sorted row list; the per-species coefficients are then loaded once for
+// all K atoms) or, with a per-atom species array, one atom (K = 1).
+template <int BLK, int K>
 __global__ void __launch_bounds__(128) k_symcon_fwd(const float* __restrict__ coef, const float* __restrict__ x,
-                                                    float* __restrict__ A, const int* __restrict__ spec, int S) {
+                                                    float* __restrict__ A, const int* __restrict__ rows, int n,
+                                                    const int* __restrict__ spec, int s0, int S) {
   constexpr int NT = BLK == 0 ? SC0_NT : SC1_NT;
   constexpr int NO = BLK == 0 ? SC0_NOUT : SC1_NOUT;
-  const int i = blockIdx.x, c = threadIdx.x;
-  const int s = min(max(spec[i], 0), S - 1);
-  float xv[16], out[NO];
-  const float* xp = x + (size_t)i * 16 * MB_C + c;
+  const int c = threadIdx.x;
+  int ri[K];
 #pragma unroll
-  for (int q = 0; q < 16; ++q) xv[q] = xp[q * MB_C];
+  for (int a = 0; a < K; ++a) {
+    const int t = blockIdx.x * K + a;
+    ri[a] = t < n ? (rows ? rows[t] : t) : -1;
+  }
+  const int s = spec ? min(max(spec[ri[0]], 0), S - 1) : s0;
+  float xv[K][16], out[K][NO];
+#pragma unroll
+  for (int a = 0; a < K; ++a) {
+    const float* xp = x + (size_t)max(ri[a], 0) * 16 * MB_C + c;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) xv[a][q] = ri[a] >= 0 ? xp[q * MB_C] : 0.f;
+  }
   const float* cf = coef + (size_t)s * NT * MB_C + c;
   if constexpr (BLK == 0)
-    sc0_fwd(xv, cf, out);
+    sc0_fwd<K>(xv, cf, out);
   else
-    sc1_fwd(xv, cf, out);
-  float* ap = A + (size_t)i * NO * MB_C + c;
+    sc1_fwd<K>(xv, cf, out);
 #pragma unroll
-  for (int q = 0; q < NO; ++q) ap[q * MB_C] = out[q];
+  for (int a = 0; a < K; ++a) {
+    if (ri[a] < 0) continue;
+    float* ap = A + (size_t)ri[a] * NO * MB_C + c;
+#pragma unroll
+    for (int q = 0; q < NO; ++q) ap[q * MB_C] = out[a][q];
+  }
 }
 
-template <int BLK>
+template <int BLK, int K>
 __global__ void __launch_bounds__(128) k_symcon_bwd(const float* __restrict__ coef, const float* __restrict__ x,
                                                     const float* __restrict__ gA, float* __restrict__ gx,
-                                                    const int* __restrict__ spec, int S, const float* __restrict__ rho,
+                                                    const int* __restrict__ rows, int n, const int* __restrict__ spec,
+                                                    int s0, int S, const float* __restrict__ rho,
                                                     float* __restrict__ grho) {
   constexpr int NT = BLK == 0 ? SC0_NT : SC1_NT;
   constexpr int NO = BLK == 0 ? SC0_NOUT : SC1_NOUT;
-  __shared__ float red4[4];
-  const int i = blockIdx.x, c = threadIdx.x;
-  const int s = min(max(spec[i], 0), S - 1);
-  float xv[16], ga[NO], gv[16];
-  const float* xp = x + (size_t)i * 16 * MB_C + c;
+  __shared__ float red[K][4];
+  const int c = threadIdx.x;
+  int ri[K];
 #pragma unroll
-  for (int q = 0; q < 16; ++q) xv[q] = xp[q * MB_C];
-  const float* gp = gA + (size_t)i * NO * MB_C + c;
+  for (int a = 0; a < K; ++a) {
+    const int t = blockIdx.x * K + a;
+    ri[a] = t < n ? (rows ? rows[t] : t) : -1;
+  }
+  const int s = spec ? min(max(spec[ri[0]], 0), S - 1) : s0;
+  float xv[K][16], ga[K][NO], gv[K][16];
 #pragma unroll
-  for (int q = 0; q < NO; ++q) ga[q] = gp[q * MB_C];
+  for (int a = 0; a < K; ++a) {
+    const size_t r = (size_t)max(ri[a], 0);
+    const float* xp = x + r * 16 * MB_C + c;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) xv[a][q] = ri[a] >= 0 ? xp[q * MB_C] : 0.f;
+    const float* gp = gA + r * NO * MB_C + c;
+#pragma unroll
+    for (int q = 0; q < NO; ++q) ga[a][q] = ri[a] >= 0 ? gp[q * MB_C] : 0.f;
+  }
   const float* cf = coef + (size_t)s * NT * MB_C + c;
   if constexpr (BLK == 0)
-    sc0_bwd(xv, cf, ga, gv);
+    sc0_bwd<K>(xv, cf, ga, gv);
   else
-    sc1_bwd(xv, cf, ga, gv);
-  float* op = gx + (size_t)i * 16 * MB_C + c;
-  float dot = 0.f;
+    sc1_bwd<K>(xv, cf, ga, gv);
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    op[q * MB_C] = gv[q];
-    dot = fmaf(gv[q], xv[q], dot);
+  for (int a = 0; a < K; ++a) {
+    float dot = 0.f;
+    if (ri[a] >= 0) {
+      float* op = gx + (size_t)ri[a] * 16 * MB_C + c;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        op[q * MB_C] = gv[a][q];
+        dot = fmaf(gv[a][q], xv[a][q], dot);
+      }
+    }
+    if (grho) {
+      dot = warp_sum(dot);
+      if ((c & 31) == 0) red[a][c >> 5] = dot;
+    }
   }
   if (grho) {
-    dot = warp_sum(dot);
-    if ((c & 31) == 0) red4[c >> 5] = dot;
     __syncthreads();
-    if (c == 0) grho[i] = -(red4[0] + red4[1] + red4[2] + red4[3]) / (rho[i] + 1.f);
+    if (c < K && ri[c] >= 0) grho[ri[c]] = -(red[c][0] + red[c][1] + red[c][2] + red[c][3]) / (rho[ri[c]] + 1.f);
   }
 }
 
@@ -277,13 +311,28 @@ __global__ void k_unpack_add(const float* __restrict__ buf, const int* __restric
   atomicAdd(dst + (int64_t)idx[k] * D + (q - k * D), buf[q]);
 }
 
+// Atoms per CTA of the species-sorted launches (register budget: x, outputs / gradients of K atoms per thread).
+#ifndef MB_SC_KF0
+#define MB_SC_KF0 4
+#endif
+#ifndef MB_SC_KF1
+#define MB_SC_KF1 8
+#endif
+#ifndef MB_SC_KB0
+#define MB_SC_KB0 2
+#endif
+#ifndef MB_SC_KB1
+#define MB_SC_KB1 4
+#endif
+constexpr int SC_K_FWD0 = MB_SC_KF0, SC_K_FWD1 = MB_SC_KF1, SC_K_BWD0 = MB_SC_KB0, SC_K_BWD1 = MB_SC_KB1;
+
 int symcon_fwd(const mb_model_t* m, int block, const float* x, float* A, const int32_t* spec, int n,
                cudaStream_t st) {
   if (n <= 0) return 0;
   if (block == 0)
-    k_symcon_fwd<0><<<n, 128, 0, st>>>(m->sc1, x, A, spec, m->S);
+    k_symcon_fwd<0, 1><<<n, 128, 0, st>>>(m->sc1, x, A, nullptr, n, spec, 0, m->S);
   else
-    k_symcon_fwd<1><<<n, 128, 0, st>>>(m->sc2, x, A, spec, m->S);
+    k_symcon_fwd<1, 1><<<n, 128, 0, st>>>(m->sc2, x, A, nullptr, n, spec, 0, m->S);
   return check_launch("symcon_fwd");
 }
 
@@ -295,10 +344,48 @@ int symcon_bwd(const mb_model_t* m, int block, const float* x, const float* gA, 
     return MB_E_ARG;
   }
   if (block == 0)
-    k_symcon_bwd<0><<<n, 128, 0, st>>>(m->sc1, x, gA, gx, spec, m->S, rho, grho);
+    k_symcon_bwd<0, 1><<<n, 128, 0, st>>>(m->sc1, x, gA, gx, nullptr, n, spec, 0, m->S, rho, grho);
   else
-    k_symcon_bwd<1><<<n, 128, 0, st>>>(m->sc2, x, gA, gx, spec, m->S, rho, grho);
+    k_symcon_bwd<1, 1><<<n, 128, 0, st>>>(m->sc2, x, gA, gx, nullptr, n, spec, 0, m->S, rho, grho);
   return check_launch("symcon_bwd");
+}
+
+// Species-sorted variants used by the chunk runners: rows = the chunk's species-sorted row list, so = its species
+// segment offsets (host, S + 1 entries); one launch per present species, K atoms per CTA.
+int symcon_fwd_sorted(const mb_model_t* m, int block, const float* x, float* A, const int32_t* rows,
+                      const int32_t* so, cudaStream_t st) {
+  for (int s = 0; s < m->S; ++s) {
+    const int n = so[s + 1] - so[s];
+    if (n <= 0) continue;
+    if (block == 0)
+      k_symcon_fwd<0, SC_K_FWD0><<<(n + SC_K_FWD0 - 1) / SC_K_FWD0, 128, 0, st>>>(m->sc1, x, A, rows + so[s], n,
+                                                                                   nullptr, s, m->S);
+    else
+      k_symcon_fwd<1, SC_K_FWD1><<<(n + SC_K_FWD1 - 1) / SC_K_FWD1, 128, 0, st>>>(m->sc2, x, A, rows + so[s], n,
+                                                                                   nullptr, s, m->S);
+    if (int rc = check_launch("symcon_fwd")) return rc;
+  }
+  return 0;
+}
+
+int symcon_bwd_sorted(const mb_model_t* m, int block, const float* x, const float* gA, float* gx,
+                      const int32_t* rows, const int32_t* so, const float* rho, float* grho, cudaStream_t st) {
+  if (grho && !rho) {
+    set_error("symcon_bwd: grho needs rho");
+    return MB_E_ARG;
+  }
+  for (int s = 0; s < m->S; ++s) {
+    const int n = so[s + 1] - so[s];
+    if (n <= 0) continue;
+    if (block == 0)
+      k_symcon_bwd<0, SC_K_BWD0><<<(n + SC_K_BWD0 - 1) / SC_K_BWD0, 128, 0, st>>>(
+          m->sc1, x, gA, gx, rows + so[s], n, nullptr, s, m->S, rho, grho);
+    else
+      k_symcon_bwd<1, SC_K_BWD1><<<(n + SC_K_BWD1 - 1) / SC_K_BWD1, 128, 0, st>>>(
+          m->sc2, x, gA, gx, rows + so[s], n, nullptr, s, m->S, rho, grho);
+    if (int rc = check_launch("symcon_bwd")) return rc;
+  }
+  return 0;
 }
 
 int readout2(const mb_model_t* m, const float* h2, double* eat, float* gh2, int n, cudaStream_t st) {

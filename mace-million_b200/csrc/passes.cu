@@ -76,6 +76,10 @@ int check_launch(const char* what) {
 }
 
 int symcon_fwd(const mb_model_t* m, int block, const float* x, float* A, const int32_t* spec, int n, cudaStream_t st);
+int symcon_fwd_sorted(const mb_model_t* m, int block, const float* x, float* A, const int32_t* rows,
+                      const int32_t* so, cudaStream_t st);
+int symcon_bwd_sorted(const mb_model_t* m, int block, const float* x, const float* gA, float* gx,
+                      const int32_t* rows, const int32_t* so, const float* rho, float* grho, cudaStream_t st);
 int symcon_bwd(const mb_model_t* m, int block, const float* x, const float* gA, float* gx, const int32_t* spec,
                const float* rho, float* grho, int n, cudaStream_t st);
 int readout2(const mb_model_t* m, const float* h2, double* eat, float* gh2, int n, cudaStream_t st);
@@ -83,6 +87,11 @@ int readout1(const mb_model_t* m, const float* H1, double* eat, int n, cudaStrea
 int gh1(const mb_model_t* m, const float* G1, float* out, int n, cudaStream_t st);
 int finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd, unsigned* fmax_bits,
              cudaStream_t st);
+
+// Species segment offsets (host, S + 1 entries) of chunk ci in its species-sorted row order.
+static inline const int32_t* chunk_so(const mb_model_t* m, const mb_eval_t* ev, int ci) {
+  return ev->spec_off + (size_t)ci * (m->S + 1);
+}
 
 #define TIMED(kind, call)                 \
   do {                                    \
@@ -204,7 +213,7 @@ extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev_all, vo
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
     TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
     RC(x1_gemms(m, ev, a, ci, st));
-    TIMED(MB_K_SYMCON, symcon_fwd(m, 0, ev->s_x, ev->s_a, ev->spec + a, nC, st));
+    TIMED(MB_K_SYMCON, symcon_fwd_sorted(m, 0, ev->s_x, ev->s_a, ev->order + a, chunk_so(m, ev, ci), st));
     GemmBatch gb(use_tc(m), ev->status, st);
     for (int l = 0; l < 2; ++l)
       RC(add(gb, {m->Wp1, m->Wp1_tc, 2 * C * C}, (size_t)l * C * C, ev->s_a, 4 * C, &kOffL[l], 1,
@@ -258,7 +267,7 @@ extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* 
       }
       RC(gb.launch());
     }
-    TIMED(MB_K_SYMCON, symcon_fwd(m, 1, ev->s_x, ev->s_a, ev->spec + a, nC, st));
+    TIMED(MB_K_SYMCON, symcon_fwd_sorted(m, 1, ev->s_x, ev->s_a, ev->order + a, chunk_so(m, ev, ci), st));
     {
       GemmBatch gb(tc, ev->status, st);   // h2 = sc + A2 Wp2 (in s_sc)
       RC(add(gb, {m->Wp2, m->Wp2_tc, C * C}, 0, ev->s_a, C, &zero, 1, ev->s_sc, C, 0, 1, nullptr, nC, nullptr, 1));
@@ -273,7 +282,8 @@ extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* 
                ev->G1 + (size_t)a * 4 * C, 4 * C, 0, 1, ev->order + a + so[s], so[s + 1] - so[s], nullptr, 1));
       RC(gb.launch());
     }
-    TIMED(MB_K_SYMCON, symcon_bwd(m, 1, ev->s_x, ev->s_ga, ev->s_gx, ev->spec + a, ev->s_rho, ev->s_grho, nC, st));
+    TIMED(MB_K_SYMCON, symcon_bwd_sorted(m, 1, ev->s_x, ev->s_ga, ev->s_gx, ev->order + a, chunk_so(m, ev, ci),
+                                         ev->s_rho, ev->s_grho, st));
     {
       GemmBatch gb(tc, ev->status, st);   // g_msg2 = g_x2 lin2^T / (rho2 + 1), one problem per mid entry
       static const int offs[4] = {0, 1, 4, 9};
@@ -318,7 +328,8 @@ extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev_all, vo
                4 * C, kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0));
       RC(gb.launch());
     }
-    TIMED(MB_K_SYMCON, symcon_bwd(m, 0, ev->s_x, ev->s_ga, ev->s_gx, ev->spec + a, ev->s_rho, ev->s_grho, nC, st));
+    TIMED(MB_K_SYMCON, symcon_bwd_sorted(m, 0, ev->s_x, ev->s_ga, ev->s_gx, ev->order + a, chunk_so(m, ev, ci),
+                                         ev->s_rho, ev->s_grho, st));
     {
       GemmBatch gb(tc, ev->status, st);   // g_msg1 = g_x1 M0[s]^T / (rho1 + 1)
       for (int l = 0; l < 4; ++l)
