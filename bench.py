@@ -49,6 +49,10 @@ FLOPS_PER_EDGE = {"edge_l1_fwd": 8 * 512 + 2 * 128 * 16 + 128 * 4,
                   "edge_l2_fwd": 8 * 1280 + 2 * 128 * 86 + 128 * 10,
                   "edge_l2_bwd": 6 * 128 * 86 + 8 * 1280}
 # edge-kernel launches per evaluation: pass A l1_fwd, pass B l2_fwd + l2_bwd, pass C l1_fwd + l1_bwd
+# DRAM traffic of one launch of the dominant kernel, from a one-pass ncu capture of this bench's own command
+# (`ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:k_edge_l2_bwd -s 10 -c 1 python bench.py
+# --steps 1 --warmup 1 --no-e2e --no-cpu-baseline`): a 16,384-receiver chunk of the 1.03M-atom water box.
+TRAFFIC_PER_LAUNCH = {("water_1m", 16384, "edge_l2_bwd"): 738.88e6 + 167.27e6}
 EDGE_PASSES = {"edge_l1_fwd": 2, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
 
 
@@ -331,7 +335,9 @@ def main():
                            "parallelism": parallelism, "gemm": "tcgen05 3xTF32" if eng.fm.use_tc else "SIMT fp32",
                            "l2": "inputs larger than L2 (no flush)"},
                 "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak, "traffic": None,
+                             "frac": achieved / peak,
+                             "traffic": TRAFFIC_PER_LAUNCH.get((args.config, args.chunk, dom)),
+                             "traffic_unit": "bytes per launch (ncu dram__bytes_read + dram__bytes_write)",
                              "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",
                              "flops_per_edge": FLOPS_PER_EDGE[dom]},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds}

@@ -28,11 +28,11 @@ __device__ __forceinline__ void set_status(unsigned* st, unsigned bit) {
 }
 
 // ---------------------------------------------------------------------------------------------- spline rows
-// Spline-coefficient loads of the edge kernels: every edge streams its own (pair, interval) row from L2 once, so
-// the rows are read through the read-only path without allocating in L1 (MB_TAB_LOAD = 1, default), or with the
-// plain read-only load (0) or L2-only caching (2).
+// Spline-coefficient loads of the edge kernels: the read-only path with L1 allocation (MB_TAB_LOAD = 0, default).
+// Measured alternatives on the 1.03M-atom evaluation: no L1 allocation (1) made the layer-2 kernels 40% slower,
+// L2-only caching (2) matched the default.
 #ifndef MB_TAB_LOAD
-#define MB_TAB_LOAD 1
+#define MB_TAB_LOAD 0
 #endif
 __device__ __forceinline__ float4 tab_ld(const float4* p) {
 #if MB_TAB_LOAD == 1
