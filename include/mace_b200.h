@@ -121,6 +121,17 @@ typedef struct {
    * instead of re-running edge_l1_fwd and the x1 GEMMs; the values are bitwise the same (deterministic kernels). */
   float* x1_cache;
   float* rho1_cache;
+  /* optional overlap of the caller's host <-> device copies with the passes (all null = off):
+   * wait_ev   HOST array [n_chunks] of cudaEvent_t: pass A makes its stream wait on wait_ev[k] before chunk k's
+   *           first kernel (the caller records it once chunk k's pair_j / rij rows are on the device);
+   * done_ev   HOST array [n_chunks] of cudaEvent_t: right after chunk k of pass C its final pair forces are written
+   *           to pf_out (fp64 [P][3] in receiver order, i.e. the caller's order for receiver-sorted input) with
+   *           their max |PF| into *fmax_bits, and done_ev[k] is recorded, so the caller can copy them out while
+   *           the next chunks run; mace_b200_finalize then converts no pair forces (energies only). */
+  void* const* wait_ev;
+  void* const* done_ev;
+  double* pf_out;
+  uint32_t* fmax_bits;
 } mb_eval_t;
 
 /* ---------------------------------------------------------------- library info */

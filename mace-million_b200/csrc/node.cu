@@ -411,8 +411,30 @@ int gh1(const mb_model_t* m, const float* G1, float* out, int n, cudaStream_t st
 
 int finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd, unsigned* fmax_bits,
              cudaStream_t st) {
-  k_finalize<<<1184, 256, 0, st>>>(ev->PF, ev->P, perm, PFd, ev->spec, m->e0, m->S, ev->nl, ev->eat, fmax_bits);
+  // with done_ev, pass C has already written every chunk's pair forces (and their max) to pf_out: energies only
+  const int64_t P = ev->done_ev ? 0 : ev->P;
+  k_finalize<<<1184, 256, 0, st>>>(ev->PF, P, perm, PFd, ev->spec, m->e0, m->S, ev->nl, ev->eat, fmax_bits);
   return check_launch("finalize");
+}
+
+// Pair forces of receivers [a, b) (edges rowptr[a] .. rowptr[b], read on the device) -> pf_out fp64, max |PF|.
+__global__ void k_pf_range(const float* __restrict__ PF, const int* __restrict__ rowptr, int a, int b,
+                           double* __restrict__ PFd, unsigned* __restrict__ fmax_bits) {
+  const int64_t e0 = rowptr[a], e1 = rowptr[b];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  unsigned mx = 0;
+  for (int64_t q = 3 * e0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < 3 * e1; q += stride) {
+    const float v = PF[q];
+    PFd[q] = (double)v;
+    mx = max(mx, __float_as_uint(fabsf(v)));
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0 && mx) atomicMax(fmax_bits, mx);
+}
+
+int pf_range(const mb_eval_t* ev, int a, int b, cudaStream_t st) {
+  k_pf_range<<<592, 256, 0, st>>>(ev->PF, ev->rowptr, a, b, ev->pf_out, ev->fmax_bits);
+  return check_launch("pf_range");
 }
 
 }  // namespace mb

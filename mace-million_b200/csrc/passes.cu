@@ -87,6 +87,7 @@ int readout1(const mb_model_t* m, const float* H1, double* eat, int n, cudaStrea
 int gh1(const mb_model_t* m, const float* G1, float* out, int n, cudaStream_t st);
 int finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd, unsigned* fmax_bits,
              cudaStream_t st);
+int pf_range(const mb_eval_t* ev, int a, int b, cudaStream_t st);
 
 // Species segment offsets (host, S + 1 entries) of chunk ci in its species-sorted row order.
 static inline const int32_t* chunk_so(const mb_model_t* m, const mb_eval_t* ev, int ci) {
@@ -211,6 +212,11 @@ extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev_all, vo
     const mb_eval_t view = chunk_view(ev_all, a);
     const mb_eval_t* ev = &view;
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
+    if (ev_all->wait_ev && ev_all->wait_ev[ci] &&
+        cudaStreamWaitEvent(st, (cudaEvent_t)ev_all->wait_ev[ci], 0) != cudaSuccess) {
+      set_error("pass_a: cudaStreamWaitEvent on wait_ev[%d] failed", ci);
+      return MB_E_CUDA;
+    }
     TIMED(MB_K_EDGE_L1_FWD, mace_b200_edge_l1_fwd(m, ev, a, b, st));
     RC(x1_gemms(m, ev, a, ci, st));
     TIMED(MB_K_SYMCON, symcon_fwd_sorted(m, 0, ev->s_x, ev->s_a, ev->order + a, chunk_so(m, ev, ci), st));
@@ -306,6 +312,10 @@ extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* 
 
 extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev_all, void* stream) {
   RC(check_pass_args(m, ev_all, "pass_c"));
+  if (ev_all->done_ev && (!ev_all->pf_out || !ev_all->fmax_bits)) {
+    set_error("pass_c: done_ev needs pf_out and fmax_bits");
+    return MB_E_ARG;
+  }
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C, S = m->S;
   const bool tc = use_tc(m);
@@ -340,6 +350,13 @@ extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev_all, vo
       RC(gb.launch());
     }
     TIMED(MB_K_EDGE_L1_BWD, mace_b200_edge_l1_bwd(m, ev, a, b, st));
+    if (ev_all->done_ev) {                     // the chunk's pair forces are final: hand them out now
+      RC(pf_range(ev_all, a, b, st));
+      if (cudaEventRecord((cudaEvent_t)ev_all->done_ev[ci], st) != cudaSuccess) {
+        set_error("pass_c: cudaEventRecord of done_ev[%d] failed", ci);
+        return MB_E_CUDA;
+      }
+    }
   }
   return 0;
 }

@@ -35,7 +35,8 @@ class MBEval(ctypes.Structure):
                 ("chunk", c_i32), ("order", c_vp), ("spec_off", c_vp),
                 ("s_msg", c_vp), ("s_x", c_vp), ("s_gx", c_vp), ("s_a", c_vp), ("s_ga", c_vp), ("s_h", c_vp),
                 ("s_gh", c_vp), ("s_sc", c_vp), ("s_rho", c_vp), ("s_grho", c_vp), ("status", c_vp),
-                ("x1_cache", c_vp), ("rho1_cache", c_vp)]
+                ("x1_cache", c_vp), ("rho1_cache", c_vp), ("wait_ev", c_vp), ("done_ev", c_vp),
+                ("pf_out", c_vp), ("fmax_bits", c_vp)]
 
 
 _SIGS = {

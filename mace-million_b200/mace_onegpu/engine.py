@@ -209,14 +209,26 @@ class Plan:
     def __init__(self, eng: "ThreePassEngine", pair_i, pair_j, rij, elems, nl: int, nt: int):
         dev = eng.device
         pi = torch.as_tensor(pair_i, device=dev).to(torch.int32)
-        pj = torch.as_tensor(pair_j, device=dev).to(torch.int32)
-        rij = torch.as_tensor(rij, device=dev).to(torch.float64)
         self.P = int(pi.numel())
         self.perm = None
-        if self.P > 1 and not bool((pi[1:] >= pi[:-1]).all()):
-            o = torch.argsort(pi, stable=True)
-            pi, pj, rij = pi[o], pj[o], rij[o]
-            self.perm = o.to(torch.int64).contiguous()
+        ordered = self.P <= 1 or bool((pi[1:] >= pi[:-1]).all())
+        # receiver-sorted pairs whose senders / vectors are still in pinned host memory: the evaluation copies them
+        # chunk by chunk on a side stream while pass A runs (host_src); otherwise they are copied (and sorted) here
+        self.host_src = None
+        pjh, rh = pair_j, rij
+        if (ordered and isinstance(pjh, torch.Tensor) and isinstance(rh, torch.Tensor) and not pjh.is_cuda
+                and not rh.is_cuda and pjh.is_pinned() and rh.is_pinned() and pjh.dtype == torch.int32
+                and rh.dtype == torch.float64 and pjh.is_contiguous() and rh.is_contiguous()):
+            self.host_src = (pjh.view(-1), rh.view(-1, 3))
+            pj = torch.empty(self.P, dtype=torch.int32, device=dev)
+            rij = torch.empty(self.P, 3, dtype=torch.float64, device=dev)
+        else:
+            pj = torch.as_tensor(pair_j, device=dev).to(torch.int32)
+            rij = torch.as_tensor(rij, device=dev).to(torch.float64)
+            if not ordered:
+                o = torch.argsort(pi, stable=True)
+                pi, pj, rij = pi[o], pj[o], rij[o]
+                self.perm = o.to(torch.int64).contiguous()
         self.pi, self.pj, self.rij = pi.contiguous(), pj.contiguous(), rij.reshape(-1, 3).contiguous()
         self.nl, self.nt = int(nl), int(nt)
         self.rowptr = torch.searchsorted(pi, torch.arange(nl + 1, device=dev, dtype=torch.int32)).to(torch.int32)
@@ -237,6 +249,8 @@ class Plan:
         off[:, 1:] = np.cumsum(cnt, 1)
         self.spec_off = np.ascontiguousarray(off.reshape(-1))
         self.n_chunks = nch
+        bounds = torch.clamp(torch.arange(nch + 1, device=dev) * C_, max=nl)
+        self.e_off = self.rowptr[bounds].to(torch.int64).cpu().numpy()   # edge range of every chunk (host)
 
 
 class ThreePassEngine:
@@ -260,6 +274,9 @@ class ThreePassEngine:
         self.col2s = col2s.to(self.device)
         self._buf = {}
         self._cap = {}
+        self._io = None                   # side stream of the host <-> device copies
+        self._ev_cache = {}
+        self.host_pf_written = False
 
     # ------------------------------------------------------------------------------------------------ buffers
     def _get(self, name, shape, dtype):
@@ -320,6 +337,11 @@ class ThreePassEngine:
         st = torch.cuda.current_stream(self.device).cuda_stream
         b["status"].zero_()
         b["eat"].zero_()
+        PFd = self._get("PFd", (plan.P, 3), torch.float64)
+        fbits = self._get("fmax", (1,), torch.int32)
+        fbits.zero_()
+        if ev.done_ev:                                   # pass C hands out every finished chunk's pair forces
+            ev.pf_out, ev.fmax_bits = N.ptr(PFd), N.ptr(fbits)
         N.check(L.mace_b200_pass_a(m, evp, st), "pass_a")
         if forward_exchange is not None and plan.nt > plan.nl:
             forward_exchange(b["H1"].view(plan.nt, 4 * C))
@@ -328,24 +350,77 @@ class ThreePassEngine:
         if reverse_exchange is not None and plan.nt > plan.nl:
             reverse_exchange(b["G1"].view(plan.nt, 4 * C))
         N.check(L.mace_b200_pass_c(m, evp, st), "pass_c")
-        PFd = self._get("PFd", (plan.P, 3), torch.float64)
-        fbits = self._get("fmax", (1,), torch.int32)
-        fbits.zero_()
         N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
         return PFd, fbits
 
+    def _events(self, key, n):
+        evs = self._ev_cache.get(key)
+        if evs is None or len(evs) < n:
+            evs = [torch.cuda.Event() for _ in range(n)]
+            cur = torch.cuda.current_stream(self.device)
+            for e in evs:                               # materialise the handles the library records / waits on
+                e.record(cur)
+            self._ev_cache[key] = evs
+        return evs[:n]
+
     def evaluate(self, plan: Plan, forward_exchange=None, reverse_exchange=None, check: bool = True,
-                 graph: bool | None = None):
+                 graph: bool | None = None, host_pf=None):
         """(eatoms fp64 [nl], pair forces dE/drij fp64 [P, 3] in the caller's pair order) on the device.
         forward_exchange(H1 [nt, 512]) fills ghost rows from their owners; reverse_exchange(G1 [nt, 512]) adds
         ghost rows onto their owners (both in place; None when nt == nl).  graph=True (or engine.graphs) replays
-        the whole evaluation as one captured CUDA graph when there is no exchange to run between the passes."""
+        the whole evaluation as one captured CUDA graph when there is no exchange to run between the passes.
+
+        Host I/O overlap: a plan whose senders / vectors are in pinned host memory (Plan.host_src) gets them copied
+        chunk by chunk on a side stream, pass A waiting per chunk; with host_pf (pinned fp64 [P, 3]) and
+        receiver-sorted input, every chunk's final pair forces are copied into host_pf as soon as pass C has
+        finished the chunk (self.host_pf_written tells whether that happened; the returned device array is then
+        complete as well)."""
+        self.host_pf_written = False
+        deferred = plan.host_src is not None
         use_graph = self.graphs if graph is None else graph
-        if use_graph and forward_exchange is None and reverse_exchange is None:
+        if use_graph and forward_exchange is None and reverse_exchange is None and not deferred:
             b, PFd, fbits = self._evaluate_graph(plan)
         else:
             ev, b = self.eval_struct(plan)
+            cur = torch.cuda.current_stream(self.device)
+            e_off, nch = plan.e_off, plan.n_chunks
+            keep = []
+            if deferred or host_pf is not None:
+                if self._io is None:
+                    self._io = torch.cuda.Stream(self.device)
+                io = self._io
+                io.wait_stream(cur)
+            if deferred:
+                h_pj, h_rij = plan.host_src
+                waits = self._events("wait", nch)
+                with torch.cuda.stream(io):
+                    for k in range(nch):
+                        e0, e1 = int(e_off[k]), int(e_off[k + 1])
+                        plan.pj[e0:e1].copy_(h_pj[e0:e1], non_blocking=True)
+                        plan.rij[e0:e1].copy_(h_rij[e0:e1], non_blocking=True)
+                        waits[k].record(io)
+                plan.pj.record_stream(io)
+                plan.rij.record_stream(io)
+                arr = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in waits])
+                keep.append(arr)
+                ev.wait_ev = N.ctypes.addressof(arr)
+            out_host = host_pf is not None and plan.perm is None and nch > 0
+            if out_host:
+                done = self._events("done", nch)
+                arr2 = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in done])
+                keep.append(arr2)
+                ev.done_ev = N.ctypes.addressof(arr2)
             PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange)
+            if out_host:
+                with torch.cuda.stream(io):
+                    for k in range(nch):
+                        e0, e1 = int(e_off[k]), int(e_off[k + 1])
+                        io.wait_event(done[k])
+                        host_pf[e0:e1].copy_(PFd[e0:e1], non_blocking=True)
+                PFd.record_stream(io)
+                self.host_pf_written = True
+            if deferred or out_host:
+                cur.wait_stream(io)
         self._last = b
         if check:
             self._check_status(b, "evaluation")

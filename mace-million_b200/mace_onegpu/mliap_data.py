@@ -32,6 +32,8 @@ class MLIAPData:
         self.host_outputs = host_outputs
         self.pair_forces = None
         self._pf_host = torch.empty((self.npairs, 3), dtype=torch.float64, pin_memory=pin) if host_outputs else None
+        # pinned host destination a force evaluation may fill directly, chunk by chunk (overlapped D2H)
+        self.pair_forces_host = self._pf_host if pin else None
         self.owner = None if owner is None else torch.as_tensor(owner).long()
         self._owner_dev = {}
         self.exchange = exchange          # distributed halo exchange (forward(H) / reverse(G) in place), e.g. domain.py
@@ -62,7 +64,8 @@ class MLIAPData:
 
     def update_pair_forces_gpu(self, PF):
         if self.host_outputs:
-            self._pf_host.copy_(PF, non_blocking=True)
+            if PF is not self._pf_host:             # else already written there by the evaluation
+                self._pf_host.copy_(PF, non_blocking=True)
             self.pair_forces = self._pf_host
         else:
             self.pair_forces = PF

@@ -117,9 +117,13 @@ class ThreePassMLIAP(MLIAPUnified):
         eng = self._eng
         dev = self._dev
         pi = torch.as_tensor(data.pair_i).to(dev, non_blocking=True)
-        pj = torch.as_tensor(data.pair_j).to(dev, non_blocking=True)
-        rij = torch.as_tensor(data.rij).to(dev, non_blocking=True)
+        pj = torch.as_tensor(data.pair_j)
+        rij = torch.as_tensor(data.rij)
+        if pj.is_cuda or rij.is_cuda or not (pj.is_pinned() and rij.is_pinned()):
+            pj, rij = pj.to(dev, non_blocking=True), rij.to(dev, non_blocking=True)
+        # pinned host senders / vectors stay on the host: the engine streams them in chunk by chunk during pass A
         plan = eng.plan(pi, pj, rij, elems.to(dev, non_blocking=True), nl, nt)
+        hbuf = getattr(data, "pair_forces_host", None)
         D = 512
 
         def fwd(H):
@@ -132,7 +136,7 @@ class ThreePassMLIAP(MLIAPUnified):
             _exchange(data.reverse_exchange, G, tmp, D)
             G.copy_(tmp)
 
-        eat, PF = eng.evaluate(plan, fwd if nt > nl else None, rev if nt > nl else None)
+        eat, PF = eng.evaluate(plan, fwd if nt > nl else None, rev if nt > nl else None, host_pf=hbuf)
         fmax = eng.fmax
         # force guard (mliap_threepass.py:595-601)
         if not (bool(torch.isfinite(eat).all()) and fmax == fmax and fmax < self._fmax_abort):
@@ -141,7 +145,7 @@ class ThreePassMLIAP(MLIAPUnified):
                                f"integrates it. The model is probably extrapolating (check the trajectory / training data).")
         torch.as_tensor(data.eatoms).copy_(eat)
         data.energy = float(eat.sum())
-        data.update_pair_forces_gpu(PF)
+        data.update_pair_forces_gpu(hbuf if eng.host_pf_written else PF)
         if self._log is not None:
             torch.cuda.synchronize()
             self._log.write(json.dumps(dict(step=self.step, nlocal=nl, ntotal=nt, npairs=P,
