@@ -116,11 +116,14 @@ __device__ __forceinline__ float transpose_reduce16(float* v, int lane) {
 // into warp-private shared memory; 4 receivers per CTA, no CTA-wide barrier.  The backward forms per lane
 // Q[lm] = sum_{its 4 channels} g[lm][c] T[l][c] and contracts it with the SH Jacobian once per 4 channels.
 constexpr int L1_WARPS = 4;
+#ifndef MB_L1_FWD_MINB
+#define MB_L1_FWD_MINB 4
+#endif
 #ifndef MB_L1_BWD_MINB
 #define MB_L1_BWD_MINB 4
 #endif
 
-__global__ void __launch_bounds__(32 * L1_WARPS) k_edge_l1_fwd(const mb_model_t m, const mb_eval_t ev, int a, int b) {
+__global__ void __launch_bounds__(32 * L1_WARPS, MB_L1_FWD_MINB) k_edge_l1_fwd(const mb_model_t m, const mb_eval_t ev, int a, int b) {
   __shared__ __align__(16) float sY[L1_WARPS][32][16];
   __shared__ int srow[L1_WARPS][32];
   __shared__ float st[L1_WARPS][32];
