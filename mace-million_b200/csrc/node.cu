@@ -2,6 +2,8 @@
 // energies, pair-force finalisation and halo row packing.
 #include <float.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm.cuh"
 #include "symcon_gen.cuh"
@@ -215,38 +217,64 @@ __global__ void __launch_bounds__(128) k_symcon_bwd(const float* __restrict__ co
 
 // ------------------------------------------------------------------------------------------------ readout 2
 // Per atom: z = h2 @ W1r, e = sum_j silu(z_j) w2r_j;  eat += scale e;  g_h2 = scale * W1r (w2r * silu'(z)).
-__global__ void __launch_bounds__(128) k_readout2(const float* __restrict__ h2, const float* __restrict__ W1r,
-                                                  const float* __restrict__ w2r, float scale, double* __restrict__ eat,
-                                                  float* __restrict__ gh2) {
-  __shared__ float sz[4][16];
-  __shared__ float sg[16];
-  const int i = blockIdx.x, c = threadIdx.x, warp = c >> 5, lane = c & 31;
-  const float h = h2[(size_t)i * MB_C + c];
-  float w[16];
+// One warp per atom (grid-stride), lane channels c = lane + 32 jj; W1r [128][16] stays in registers (64 per lane)
+// across the warp's atoms.  z_j = sum_c h_c W1r[c][j] is reduced over the warp with a 16-value transpose reduction
+// (lane L ends with z_{L >> 1}); e = sum_j silu(z_j) w2r_j;  g_h2[c] = scale sum_j W1r[c][j] w2r_j silu'(z_j).
+__device__ __forceinline__ float readout_tr16(float* v, int lane) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    w[j] = __ldg(W1r + c * 16 + j);
-    float z = warp_sum(h * w[j]);
-    if (lane == 0) sz[warp][j] = z;
-  }
-  __syncthreads();
-  if (c < 32) {
-    float e = 0.f;
-    if (c < 16) {
-      const float z = sz[0][c] + sz[1][c] + sz[2][c] + sz[3][c];
-      const float sig = 1.f / (1.f + expf(-z));
-      const float w2 = __ldg(w2r + c);
-      e = z * sig * w2;
-      sg[c] = scale * w2 * sig * (1.f + z * (1.f - sig));
+  for (int h = 8, bit = 16; h >= 1; h >>= 1, bit >>= 1) {
+    const bool up = lane & bit;
+#pragma unroll
+    for (int q = 0; q < h; ++q) {
+      const float send = up ? v[q] : v[q + h];
+      const float keep = up ? v[q + h] : v[q];
+      v[q] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
     }
-    e = warp_sum(e);
-    if (c == 0) eat[i] += (double)scale * (double)e;
   }
-  __syncthreads();
-  float g = 0.f;
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+__global__ void __launch_bounds__(256) k_readout2(const float* __restrict__ h2, const float* __restrict__ W1r,
+                                                  const float* __restrict__ w2r, float scale, double* __restrict__ eat,
+                                                  float* __restrict__ gh2, int n) {
+  const int lane = threadIdx.x & 31;
+  const int warp0 = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int nwarps = (int)(((int64_t)gridDim.x * blockDim.x) >> 5);
+  float w[4][16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) g = fmaf(sg[j], w[j], g);
-  gh2[(size_t)i * MB_C + c] = g;
+  for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[jj][j] = __ldg(W1r + (lane + 32 * jj) * 16 + j);
+  const int jl = lane >> 1;                      // the z component this lane ends with
+  const float w2 = __ldg(w2r + jl);
+  for (int i = warp0; i < n; i += nwarps) {
+    float h[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) h[jj] = h2[(size_t)i * MB_C + lane + 32 * jj];
+    float z[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float t = h[0] * w[0][j];
+#pragma unroll
+      for (int jj = 1; jj < 4; ++jj) t = fmaf(h[jj], w[jj][j], t);
+      z[j] = t;
+    }
+    const float zj = readout_tr16(z, lane);
+    const float sig = 1.f / (1.f + expf(-zj));
+    float e = (lane & 1) ? 0.f : zj * sig * w2;  // one lane of each pair
+    const float sg = scale * w2 * sig * (1.f + zj * (1.f - sig));
+    e = warp_sum(e);
+    if (lane == 0) eat[i] += (double)scale * (double)e;
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float sj = __shfl_sync(0xffffffffu, sg, 2 * j);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) g[jj] = fmaf(sj, w[jj][j], g[jj]);
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) gh2[(size_t)i * MB_C + lane + 32 * jj] = g[jj];
+  }
 }
 
 // R1 energies: eat[i] += scale * H1[i][0][:] . wr0
@@ -392,7 +420,8 @@ int symcon_bwd_sorted(const mb_model_t* m, int block, const float* x, const floa
 
 int readout2(const mb_model_t* m, const float* h2, double* eat, float* gh2, int n, cudaStream_t st) {
   if (n <= 0) return 0;
-  k_readout2<<<n, 128, 0, st>>>(h2, m->W1r, m->w2r, m->scale, eat, gh2);
+  const int blocks = (int)std::min<int64_t>(((int64_t)n + 7) / 8, 148 * 8);   // 8 warps per CTA, grid-stride
+  k_readout2<<<blocks, 256, 0, st>>>(h2, m->W1r, m->w2r, m->scale, eat, gh2, n);
   return check_launch("readout2");
 }
 
