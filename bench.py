@@ -196,9 +196,13 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa = False
     if world > 1:
         import datetime
 
+        from mace_onegpu import hostio
+
+        numa = hostio.bind_to_gpu_numa(dev)    # pinned e2e buffers on the GPU's NUMA node (first touch)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     def barrier():
@@ -333,6 +337,7 @@ def main():
                            "atoms_rank0": n, "ghosts_rank0": nt - n, "pairs_rank0": P, "chunk": args.chunk,
                            "spline_knots": 512, "model": "MACE-MPA-0-medium architecture, random init",
                            "parallelism": parallelism, "gemm": "tcgen05 3xTF32" if eng.fm.use_tc else "SIMT fp32",
+                           "host_numa_bound": numa,
                            "l2": "inputs larger than L2 (no flush)"},
                 "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak,

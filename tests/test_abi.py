@@ -37,3 +37,10 @@ def test_sc_layout_query():
     assert N.lib().mace_b200_sc_layout(1, N.byref(n), N.byref(fp)) == 0 and n.value == 94
     assert N.lib().mace_b200_sc_layout(7, N.byref(n), N.byref(fp)) != 0
     assert b"block" in N.lib().mace_b200_last_error()
+
+
+def test_hostio_cpulist_parsing():
+    from mace_onegpu import hostio
+
+    assert hostio._parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert hostio._parse_cpulist("") == set()
