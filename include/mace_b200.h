@@ -48,8 +48,8 @@ typedef struct {
   int32_t C, S, M;             /* channels, species, spline knots */
   float r_lo, inv_h, r_max, p_cut;
   float scale;                 /* ScaleShift scale */
-  const float* tab1;           /* [S*S][M-1][4][C] float4 cubic coefficients of W1 * X1(sender species) */
-  const float* tab2;           /* [S*S][M-1][10][C] float4 cubic coefficients of W2 */
+  const float* tab1;           /* [T1][M-1][4][C] float4 cubic coefficients of W1 * X1(sender species), T1 tables */
+  const float* tab2;           /* [T2][M-1][10][C] float4 cubic coefficients of W2, T2 tables (see tab*_map) */
   const float* wd1;            /* [8] layer-1 density weights / sqrt(8) */
   const float* wd2;            /* [8] layer-2 density weights / sqrt(8) */
   const float* M0;             /* [S][4][C][C]  linear_1 o skip_tp_1 per species and l */
@@ -85,6 +85,11 @@ typedef struct {
   const float* Wp2_tc;
   const float* Wp2T_tc;
   int32_t use_tc;              /* node GEMMs on tcgen05 (3xTF32) instead of the SIMT fp32 kernel */
+  /* optional [S*S] maps from the ordered species pair (sender * S + receiver) to the table of tab1 / tab2 it reads
+   * (null = identity).  Pairs whose tables are bitwise identical share one table: W2 has no species dependence in
+   * an architecture without a species-pair distance transform, W1 * X1 depends on the sender species only. */
+  const int32_t* tab1_map;
+  const int32_t* tab2_map;
 } mb_model_t;
 
 /* One force evaluation: the pair list (receiver-sorted), persistent per-atom state and per-chunk scratch. */

@@ -56,6 +56,9 @@ __device__ __forceinline__ bool edge_geom(const mb_eval_t& ev, const EdgeCtx& x,
   return true;
 }
 
+// Table index of an ordered species pair (bitwise-identical per-pair tables share one table; null map = identity).
+__device__ __forceinline__ int table_of(int pair, const int32_t* map) { return map ? __ldg(map + pair) : pair; }
+
 __device__ __forceinline__ bool row_range(const mb_eval_t& ev, int i, int64_t& e0, int64_t& e1) {
   e0 = ev.rowptr[i];
   e1 = ev.rowptr[i + 1];
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1_FWD_MINB) k_edge_l1_fwd(c
         int k;
         float t;
         spline_coords(r, x.rd, k, t);
-        row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
+        row = (table_of(pair, m.tab1_map) * (x.rd.M - 1) + k) * 4 * MB_C;
         st[warp][lane] = t;
         const float ir = 1.f / r;
         float Y[16];
@@ -230,7 +233,7 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1_BWD_MINB) k_edge_l1_bwd(c
         int k;
         float t;
         spline_coords(r, x.rd, k, t);
-        row = (pair * (x.rd.M - 1) + k) * 4 * MB_C;
+        row = (table_of(pair, m.tab1_map) * (x.rd.M - 1) + k) * 4 * MB_C;
         st[warp][lane] = t;
         const float ir = 1.f / r;
         sh16<float>(v.x * ir, v.y * ir, v.z * ir, sY[warp][lane]);
@@ -357,7 +360,7 @@ __global__ void __launch_bounds__(128, MB_L2_FWD_MINB) k_edge_l2_fwd(const mb_mo
         int k;
         float t;
         spline_coords(r, x.rd, k, t);
-        row = (pair * (x.rd.M - 1) + k) * TP2_NW * MB_C;
+        row = (table_of(pair, m.tab2_map) * (x.rd.M - 1) + k) * TP2_NW * MB_C;
         st[c] = t;
         ssend[c] = j;
         const float ir = 1.f / r;
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(128, MB_L2_BWD_MINB) k_edge_l2_bwd(const mb_mo
         int k;
         float t;
         spline_coords(r, x.rd, k, t);
-        row = (pair * (x.rd.M - 1) + k) * TP2_NW * MB_C;
+        row = (table_of(pair, m.tab2_map) * (x.rd.M - 1) + k) * TP2_NW * MB_C;
         st[c] = t;
         ssend[c] = j;
         const float ir = 1.f / r;

@@ -25,7 +25,7 @@ class MBModel(ctypes.Structure):
                 ("sc2", c_vp), ("Wp2", c_vp), ("Wp2T", c_vp), ("W1r", c_vp), ("w2r", c_vp), ("e0", c_vp),
                 ("M0_tc", c_vp), ("M0T_tc", c_vp), ("Wp1_tc", c_vp), ("Wp1T_tc", c_vp), ("Wup2_tc", c_vp),
                 ("Wup2T_tc", c_vp), ("Wsk1_tc", c_vp), ("Wsk1T_tc", c_vp), ("Wlin2_tc", c_vp), ("Wlin2T_tc", c_vp),
-                ("Wp2_tc", c_vp), ("Wp2T_tc", c_vp), ("use_tc", c_i32)]
+                ("Wp2_tc", c_vp), ("Wp2T_tc", c_vp), ("use_tc", c_i32), ("tab1_map", c_vp), ("tab2_map", c_vp)]
 
 
 class MBEval(ctypes.Structure):

@@ -72,6 +72,25 @@ def tc_planes(B: np.ndarray) -> np.ndarray:
     return out.reshape(planes.shape)
 
 
+def dedup_tables(cub: torch.Tensor):
+    """Per-pair spline tables [S*S, ...] -> (distinct tables [T, ...], int32 map [S*S] pair -> table).  Tables are
+    merged only when bitwise identical, so the kernels read exactly the values they would read per pair; a model
+    whose radial weights depend on the species pair keeps all S*S tables."""
+    reps, idx = [], []
+    for p in range(cub.shape[0]):
+        for u, q in enumerate(reps):
+            if torch.equal(cub[p], cub[q]):
+                idx.append(u)
+                break
+        else:
+            reps.append(p)
+            idx.append(len(reps) - 1)
+    tmap = torch.as_tensor(idx, dtype=torch.int32, device=cub.device)
+    if len(reps) == cub.shape[0]:
+        return cub, tmap
+    return cub[reps].contiguous(), tmap
+
+
 def fold_weights(model: Mdl.MACEModel, cols) -> dict:
     """All folded fp64 arrays (CPU numpy) for the species columns `cols` (model one-hot columns present)."""
     a = model.arch
@@ -192,7 +211,9 @@ class FoldedModel:
                                              A[0].shape[1], D, N.ptr(cs), S * S, self.M, self.r_lo, self.r_max,
                                              float(a.num_poly_cutoff), N.ptr(TV), N.ptr(TG), N.ptr(cub), st),
                     "build_tables")
+            cub, tmap = dedup_tables(cub)
             t[key] = cub
+            t[key + "_map"] = tmap
             self.TV[i], self.TG[i] = TV, TG
             t[f"_A{i}"] = A
         self.t = t

@@ -131,3 +131,14 @@ def test_tc_planes_are_the_swizzled_split():
     assert planes.shape == split.shape
     back = planes.reshape(-1, 128 * 128)[:, pos].reshape(split.shape)
     assert np.array_equal(back, split)
+
+
+def test_dedup_tables_merges_only_identical():
+    a = torch.randn(3, 5, 4)
+    cub = torch.stack([a[0], a[1], a[0], a[2], a[1].clone()])
+    cub[4, 2, 1] += 1e-7                       # one ulp-scale difference keeps its own table
+    t, m = E.dedup_tables(cub)
+    assert m.tolist() == [0, 1, 0, 2, 3]
+    assert t.shape[0] == 4
+    for p in range(cub.shape[0]):
+        assert torch.equal(t[m[p]], cub[p])

@@ -67,6 +67,18 @@ def test_tables_match_oracle(mdl, water, oracle):
             assert (tg[0] - rt["TG"]).abs().max() <= 1e-6 * rt["TG"].abs().max() + 1e-9
 
 
+def test_tables_shared_across_identical_pairs(mdl, water):
+    """W2 does not depend on the species pair in this architecture, W1 * X1 only on the sender: water (S = 2) keeps
+    one layer-2 and two layer-1 tables, and every pair maps to the right one."""
+    eng = _engine(mdl, water["cols"], 64)
+    t, S_ = eng.fm.t, eng.fm.S
+    assert t["tab2"].shape[0] == 1 and t["tab2_map"].tolist() == [0] * (S_ * S_)
+    assert t["tab1"].shape[0] == S_
+    m1 = t["tab1_map"].view(S_, S_)
+    assert all(len(set(m1[s].tolist())) == 1 for s in range(S_))       # row = sender species
+    assert len(set(m1[:, 0].tolist())) == S_
+
+
 def _run(eng, water, owner=None, nt=None, pj=None):
     nt = water["n"] if nt is None else nt
     pj = water["pj"] if pj is None else pj
