@@ -48,12 +48,16 @@ FLOPS_PER_EDGE = {"edge_l1_fwd": 8 * 512 + 2 * 128 * 16 + 128 * 4,
                   "edge_l1_bwd": 4 * 128 * 16 + 8 * 512,
                   "edge_l2_fwd": 8 * 1280 + 2 * 128 * 86 + 128 * 10,
                   "edge_l2_bwd": 6 * 128 * 86 + 8 * 1280}
-# edge-kernel launches per evaluation: pass A l1_fwd, pass B l2_fwd + l2_bwd, pass C l1_fwd + l1_bwd
+# the density-projection layer 1 (64 hidden features per edge instead of 4 C weights): forward 8 H + 2 H 16,
+# backward 8 H + 4 H 16, H = 64
+FLOPS_PER_EDGE_L1D = {"edge_l1_fwd": 8 * 64 + 2 * 64 * 16, "edge_l1_bwd": 8 * 64 + 4 * 64 * 16}
+# edge-kernel launches per evaluation: pass A l1_fwd, pass B l2_fwd + l2_bwd, pass C l1_bwd (pass C reads pass A's
+# layer-1 results from the x1 cache, which the engine keeps whenever it fits)
 # DRAM traffic of one launch of the dominant kernel, from a one-pass ncu capture of this bench's own command
 # (`ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:k_edge_l2_bwd -s 10 -c 1 python bench.py
 # --steps 1 --warmup 1 --no-e2e --no-cpu-baseline`): a 16,384-receiver chunk of the 1.03M-atom water box.
 TRAFFIC_PER_LAUNCH = {("water_1m", 16384, "edge_l2_bwd"): 738.88e6 + 167.27e6}
-EDGE_PASSES = {"edge_l1_fwd": 2, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
+EDGE_PASSES = {"edge_l1_fwd": 1, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
 
 
 def parse():
@@ -282,9 +286,10 @@ def main():
     value = n_total * args.steps / (ms * 1e-3)
 
     # roofline of the dominant kernel (FP32 SIMT edge kernels: FLOP/s against the measured FFMA issue ceiling)
-    dom = max((k for k in kern if k in FLOPS_PER_EDGE), key=lambda k: kern[k][0])
+    fpe = dict(FLOPS_PER_EDGE, **(FLOPS_PER_EDGE_L1D if eng.fm.l1_density else {}))
+    dom = max((k for k in kern if k in fpe), key=lambda k: kern[k][0])
     dom_ms, dom_launches = kern[dom]
-    flops = FLOPS_PER_EDGE[dom] * P * EDGE_PASSES[dom] * args.steps
+    flops = fpe[dom] * P * EDGE_PASSES[dom] * args.steps
     achieved = flops / (dom_ms * 1e-3) / 1e12 if dom_ms > 0 else 0.0
     scratch = torch.zeros(1, device=dev)
     pk = N.c_f64()
@@ -337,6 +342,7 @@ def main():
                            "atoms_rank0": n, "ghosts_rank0": nt - n, "pairs_rank0": P, "chunk": args.chunk,
                            "spline_knots": 512, "model": "MACE-MPA-0-medium architecture, random init",
                            "parallelism": parallelism, "gemm": "tcgen05 3xTF32" if eng.fm.use_tc else "SIMT fp32",
+                           "layer1": "density projection" if eng.fm.l1_density else "direct",
                            "host_numa_bound": numa,
                            "l2": "inputs larger than L2 (no flush)"},
                 "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -344,7 +350,7 @@ def main():
                              "traffic": TRAFFIC_PER_LAUNCH.get((args.config, args.chunk, dom)),
                              "traffic_unit": "bytes per launch (ncu dram__bytes_read + dram__bytes_write)",
                              "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",
-                             "flops_per_edge": FLOPS_PER_EDGE[dom]},
+                             "flops_per_edge": fpe[dom]},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define MB_ABI_VERSION 1
+#define MB_ABI_VERSION 2
 
 enum {
   MB_OK = 0,
@@ -48,11 +48,14 @@ typedef struct {
   int32_t C, S, M;             /* channels, species, spline knots */
   float r_lo, inv_h, r_max, p_cut;
   float scale;                 /* ScaleShift scale */
-  const float* tab1;           /* [T1][M-1][4][C] float4 cubic coefficients of W1 * X1(sender species), T1 tables */
+  const float* tab1;           /* [T1][M-1][4][C] float4 cubic coefficients of W1 * X1(sender species), T1 tables;
+                                  with l1_density: [M-1][64] float4 cubic coefficients of the radial MLP's last
+                                  hidden layer h(r) */
   const float* tab2;           /* [T2][M-1][10][C] float4 cubic coefficients of W2, T2 tables (see tab*_map) */
   const float* wd1;            /* [8] layer-1 density weights / sqrt(8) */
   const float* wd2;            /* [8] layer-2 density weights / sqrt(8) */
-  const float* M0;             /* [S][4][C][C]  linear_1 o skip_tp_1 per species and l */
+  const float* M0;             /* [S][4][C][C]  linear_1 o skip_tp_1 per species and l; with l1_density the
+                                  composite [S][4][2 x 64][C] = (last MLP layer x X1 of species slot) o M0 */
   const float* M0T;            /* transposes */
   const float* Wp1;            /* [2][C][C]     products[0].linear per l */
   const float* Wp1T;
@@ -90,6 +93,10 @@ typedef struct {
    * an architecture without a species-pair distance transform, W1 * X1 depends on the sender species only. */
   const int32_t* tab1_map;
   const int32_t* tab2_map;
+  /* exact density-projection layer 1 (S <= 2): the layer-1 edge kernels accumulate per receiver the densities
+   * B[m][slot * 64 + q] = sum over edges from species `slot` of h_q(r) Y_m into the message rows of the chunk
+   * (instead of msg1[m][c]) and the backward reads dE/dB there; M0 / M0T map B to x1 directly.  0 = direct. */
+  int32_t l1_density;
 } mb_model_t;
 
 /* One force evaluation: the pair list (receiver-sorted), persistent per-atom state and per-chunk scratch. */

@@ -314,6 +314,218 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1_BWD_MINB) k_edge_l1_bwd(c
   }
 }
 
+// ------------------------------------------------------------------------------------------------ layer 1, density form
+// Exact density projection of layer 1 (mb_model_t.l1_density, S <= 2; derived in the reference's
+// mace_onegpu/ace_layer1.py:2-16).  The layer-1 sender features depend only on the sender species and the radial
+// MLP's last layer is linear, so the per-receiver densities B[s][q][m] = sum_{e: s_e = s} h_q(r_e) Y_m(e) of the 64
+// hidden features h carry the whole message; the chunk's node GEMM (composite M0) maps them to x1.  One warp per
+// receiver, lane = hidden features lane and lane + 32: per edge two 16-byte loads of a 64-column table (one table
+// for every pair) instead of sixteen of a 512-column one, and 32 message FMAs per lane instead of 64.  The batch
+// prologue orders the batch's edges by sender species (ballot prefix), so each species slot runs its own loop with
+// its accumulators in registers and no per-edge branch.
+constexpr int L1D_H = 64;
+#ifndef MB_L1D_FWD_MINB
+#define MB_L1D_FWD_MINB 4
+#endif
+#ifndef MB_L1D_BWD_MINB
+#define MB_L1D_BWD_MINB 4
+#endif
+
+// Position of this lane's edge in the species-ordered batch (slot 0 first); returns the slot-0 count in n0 and the
+// number of valid edges in nv.  Every lane of the warp calls it.
+__device__ __forceinline__ int l1d_slot_order(bool ok, int slot, int lane, int& n0, int& nv) {
+  const unsigned all = __ballot_sync(0xffffffffu, ok);
+  const unsigned m1 = __ballot_sync(0xffffffffu, ok && slot == 1);
+  const unsigned m0 = all & ~m1;
+  const unsigned lt = (1u << lane) - 1u;
+  n0 = __popc(m0);
+  nv = __popc(all);
+  return slot == 1 ? n0 + __popc(m1 & lt) : __popc(m0 & lt);
+}
+
+__device__ __forceinline__ void l1d_accumulate(float (&B)[2][16], const float4* rw, float t, const float* y) {
+  const float h0 = cubic(tab_ld(rw), t), h1 = cubic(tab_ld(rw + 32), t);
+#pragma unroll
+  for (int k = 0; k < 16; k += 4) {
+    const float4 y4 = *reinterpret_cast<const float4*>(y + k);
+    const float Y[4] = {y4.x, y4.y, y4.z, y4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      B[0][k + u] = fmaf(h0, Y[u], B[0][k + u]);
+      B[1][k + u] = fmaf(h1, Y[u], B[1][k + u]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_FWD_MINB) k_edge_l1d_fwd(const mb_model_t m, const mb_eval_t ev,
+                                                                                int a, int b) {
+  __shared__ __align__(16) float sY[L1_WARPS][32][16];
+  __shared__ int srow[L1_WARPS][32];
+  __shared__ float st[L1_WARPS][32];
+  const EdgeCtx x = make_ctx(m, ev);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int il = blockIdx.x * L1_WARPS + warp, i = a + il;
+  if (i >= b) return;
+  int64_t e0, e1;
+  if (!row_range(ev, i, e0, e1)) return;
+  const float4* tab = reinterpret_cast<const float4*>(m.tab1) + lane;
+  float B0[2][16], B1[2][16];        // densities of species slot 0 / 1: [hidden feature lane + 32 hh][m]
+#pragma unroll
+  for (int q = 0; q < 16; ++q) B0[0][q] = B0[1][q] = B1[0][q] = B1[1][q] = 0.f;
+  float rho = 0.f;
+  for (int64_t base = e0; base < e1; base += 32) {
+    const int n = (int)min((int64_t)32, e1 - base);
+    float3 v;
+    float r = 0.f;
+    int j, pair = 0;
+    const bool ok = lane < n && edge_geom(ev, x, base + lane, i, v, r, j, pair);
+    const int slot = ok ? pair / x.S : 0;
+    int n0, nv;
+    const int pos = l1d_slot_order(ok, slot, lane, n0, nv);
+    if (ok) {
+      int k;
+      float t;
+      spline_coords(r, x.rd, k, t);
+      srow[warp][pos] = k * L1D_H;
+      st[warp][pos] = t;
+      const float ir = 1.f / r;
+      sh16<float>(v.x * ir, v.y * ir, v.z * ir, sY[warp][pos]);
+      float ed, ded;
+      edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
+      rho += ed;
+    }
+    __syncwarp();
+    for (int q = 0; q < n0; ++q) l1d_accumulate(B0, tab + srow[warp][q], st[warp][q], sY[warp][q]);
+    for (int q = n0; q < nv; ++q) l1d_accumulate(B1, tab + srow[warp][q], st[warp][q], sY[warp][q]);
+    __syncwarp();
+  }
+  float* out = ev.s_msg + (size_t)il * 16 * MB_C + lane;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    out[q * MB_C] = B0[0][q];
+    out[q * MB_C + 32] = B0[1][q];
+    out[q * MB_C + 64] = B1[0][q];
+    out[q * MB_C + 96] = B1[1][q];
+  }
+  rho = warp_sum(rho);
+  if (lane == 0) ev.s_rho[il] = rho;
+}
+
+// One edge of the density backward: from g = dE/dB of the edge's species slot, dE/dh_q = sum_m g[q][m] Y_m (into
+// the spline derivative) and this lane's share of dE/dY_m = sum_q g[q][m] h_q, reduced over the warp into sred.
+__device__ __forceinline__ void l1d_edge_bwd(const float (&g)[2][16], const float4* rw, float t, const float* y,
+                                             float* sred_row, int lane) {
+  const float4 c0 = tab_ld(rw), c1 = tab_ld(rw + 32);
+  const float h0 = cubic(c0, t), h1 = cubic(c1, t);
+  float Y[16];
+#pragma unroll
+  for (int k = 0; k < 16; k += 4) {
+    const float4 y4 = *reinterpret_cast<const float4*>(y + k);
+    Y[k] = y4.x;
+    Y[k + 1] = y4.y;
+    Y[k + 2] = y4.z;
+    Y[k + 3] = y4.w;
+  }
+  float Q[16];
+  float G0a = 0.f, G0b = 0.f, G1a = 0.f, G1b = 0.f;
+#pragma unroll
+  for (int mm = 0; mm < 16; mm += 2) {
+    G0a = fmaf(g[0][mm], Y[mm], G0a);
+    G1a = fmaf(g[1][mm], Y[mm], G1a);
+    G0b = fmaf(g[0][mm + 1], Y[mm + 1], G0b);
+    G1b = fmaf(g[1][mm + 1], Y[mm + 1], G1b);
+  }
+#pragma unroll
+  for (int mm = 1; mm < 16; ++mm) Q[mm] = fmaf(g[0][mm], h0, g[1][mm] * h1);
+  const float G0 = G0a + G0b, G1 = G1a + G1b;
+  const float Sb = fmaf(G0, c0.y, G1 * c1.y), Sc = fmaf(G0, c0.z, G1 * c1.z), Sd = fmaf(G0, c0.w, G1 * c1.w);
+  Q[0] = fmaf(t, fmaf(3.f * t, Sd, 2.f * Sc), Sb);   // dE/dt of this lane's hidden features (Y_0 is constant)
+  const float s = transpose_reduce16(Q, lane);
+  if ((lane & 1) == 0) sred_row[lane >> 1] = s;
+}
+
+__global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_BWD_MINB) k_edge_l1d_bwd(const mb_model_t m, const mb_eval_t ev,
+                                                                                int a, int b) {
+  __shared__ __align__(16) float sY[L1_WARPS][32][16];
+  __shared__ __align__(16) float sred[L1_WARPS][32][17];
+  __shared__ __align__(16) float sv[L1_WARPS][32][4];
+  __shared__ float sgd[L1_WARPS][32];
+  __shared__ int srow[L1_WARPS][32];
+  __shared__ int sedge[L1_WARPS][32];
+  __shared__ float st[L1_WARPS][32];
+  const EdgeCtx x = make_ctx(m, ev);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int il = blockIdx.x * L1_WARPS + warp, i = a + il;
+  if (i >= b) return;
+  int64_t e0, e1;
+  if (!row_range(ev, i, e0, e1)) return;
+  const float4* tab = reinterpret_cast<const float4*>(m.tab1) + lane;
+  // dE/dB of this receiver, [m][slot * 64 + hh * 32 + lane]; each slot's 32 values are loaded (L1 hits after the
+  // first batch) before that slot's edge loop, so that only one slot occupies registers
+  const float* gin = ev.s_msg + (size_t)il * 16 * MB_C + lane;
+  const float grho = ev.s_grho[il];
+  for (int64_t base = e0; base < e1; base += 32) {
+    const int n = (int)min((int64_t)32, e1 - base);
+    float3 v;
+    float r = 0.f;
+    int j, pair = 0;
+    const bool ok = lane < n && edge_geom(ev, x, base + lane, i, v, r, j, pair);
+    const int slot = ok ? pair / x.S : 0;
+    int n0, nv;
+    const int pos = l1d_slot_order(ok, slot, lane, n0, nv);
+    if (ok) {
+      int k;
+      float t;
+      spline_coords(r, x.rd, k, t);
+      srow[warp][pos] = k * L1D_H;
+      st[warp][pos] = t;
+      sedge[warp][pos] = lane;
+      const float ir = 1.f / r;
+      sh16<float>(v.x * ir, v.y * ir, v.z * ir, sY[warp][pos]);
+      float ed, ded;
+      edge_density(r, m.wd1, x.rd.r_max, x.rd.p, ed, ded);
+      sv[warp][pos][0] = v.x;
+      sv[warp][pos][1] = v.y;
+      sv[warp][pos][2] = v.z;
+      sv[warp][pos][3] = r;
+      sgd[warp][pos] = grho * ded;
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int slot = 0; slot < 2; ++slot) {
+      const int q0 = slot ? n0 : 0, q1 = slot ? nv : n0;
+      if (q0 == q1) continue;
+      float g[2][16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        g[0][q] = gin[q * MB_C + slot * 64];
+        g[1][q] = gin[q * MB_C + slot * 64 + 32];
+      }
+      for (int q = q0; q < q1; ++q) l1d_edge_bwd(g, tab + srow[warp][q], st[warp][q], sY[warp][q], sred[warp][q], lane);
+    }
+    __syncwarp();
+    if (lane < nv) {
+      const float* gs = sred[warp][lane];
+      const float r = sv[warp][lane][3], ir = 1.f / r;
+      const float3 u = make_float3(sv[warp][lane][0] * ir, sv[warp][lane][1] * ir, sv[warp][lane][2] * ir);
+      float Yj[16], J[48];
+      sh_jacobian(u, r, Yj, J);
+      const float gr = fmaf(gs[0], x.rd.inv_h, sgd[warp][lane]);
+      float f[3] = {gr * u.x, gr * u.y, gr * u.z};
+#pragma unroll
+      for (int mm = 1; mm < 16; ++mm) {
+        f[0] = fmaf(gs[mm], J[3 * mm + 0], f[0]);
+        f[1] = fmaf(gs[mm], J[3 * mm + 1], f[1]);
+        f[2] = fmaf(gs[mm], J[3 * mm + 2], f[2]);
+      }
+      float* pf = ev.PF + 3 * (base + sedge[warp][lane]);
+#pragma unroll
+      for (int d = 0; d < 3; ++d) pf[d] += f[d];
+    }
+    __syncwarp();
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ layer 2 forward
 // Resident CTAs per SM the layer-2 kernels are compiled for (register budget 65536 / (128 x MINB) per thread).
 #ifndef MB_L2_FWD_MINB
@@ -538,6 +750,10 @@ static int edge_args(const mb_model_t* m, const mb_eval_t* ev, int a, int b, con
     set_error("%s: only C = 128 is supported (got %d)", who, m->C);
     return MB_E_ARG;
   }
+  if (m->l1_density && (m->S < 1 || m->S > 2)) {
+    set_error("%s: the density-projection layer 1 supports 1 or 2 species (got %d)", who, m->S);
+    return MB_E_ARG;
+  }
   return 0;
 }
 
@@ -548,14 +764,22 @@ using namespace mb;
 extern "C" int mace_b200_edge_l1_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
   if (int rc = edge_args(m, ev, a, b, "edge_l1_fwd")) return rc;
   if (b == a) return 0;
-  k_edge_l1_fwd<<<(b - a + L1_WARPS - 1) / L1_WARPS, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
+  const int grid = (b - a + L1_WARPS - 1) / L1_WARPS;
+  if (m->l1_density)
+    k_edge_l1d_fwd<<<grid, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
+  else
+    k_edge_l1_fwd<<<grid, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
   return check_launch("edge_l1_fwd");
 }
 
 extern "C" int mace_b200_edge_l1_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
   if (int rc = edge_args(m, ev, a, b, "edge_l1_bwd")) return rc;
   if (b == a) return 0;
-  k_edge_l1_bwd<<<(b - a + L1_WARPS - 1) / L1_WARPS, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
+  const int grid = (b - a + L1_WARPS - 1) / L1_WARPS;
+  if (m->l1_density)
+    k_edge_l1d_bwd<<<grid, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
+  else
+    k_edge_l1_bwd<<<grid, 32 * L1_WARPS, 0, (cudaStream_t)stream>>>(*m, *ev, a, b);
   return check_launch("edge_l1_bwd");
 }
 

@@ -16,6 +16,9 @@ c_i32, c_i64, c_u32, c_u64, c_f32, c_f64 = (ctypes.c_int32, ctypes.c_int64, ctyp
 c_vp = ctypes.c_void_p
 
 
+ABI_VERSION = 2          # MB_ABI_VERSION of include/mace_b200.h this binding mirrors
+
+
 class MBModel(ctypes.Structure):
     _fields_ = [("C", c_i32), ("S", c_i32), ("M", c_i32),
                 ("r_lo", c_f32), ("inv_h", c_f32), ("r_max", c_f32), ("p_cut", c_f32), ("scale", c_f32),
@@ -25,7 +28,8 @@ class MBModel(ctypes.Structure):
                 ("sc2", c_vp), ("Wp2", c_vp), ("Wp2T", c_vp), ("W1r", c_vp), ("w2r", c_vp), ("e0", c_vp),
                 ("M0_tc", c_vp), ("M0T_tc", c_vp), ("Wp1_tc", c_vp), ("Wp1T_tc", c_vp), ("Wup2_tc", c_vp),
                 ("Wup2T_tc", c_vp), ("Wsk1_tc", c_vp), ("Wsk1T_tc", c_vp), ("Wlin2_tc", c_vp), ("Wlin2T_tc", c_vp),
-                ("Wp2_tc", c_vp), ("Wp2T_tc", c_vp), ("use_tc", c_i32), ("tab1_map", c_vp), ("tab2_map", c_vp)]
+                ("Wp2_tc", c_vp), ("Wp2T_tc", c_vp), ("use_tc", c_i32), ("tab1_map", c_vp), ("tab2_map", c_vp),
+                ("l1_density", c_i32)]
 
 
 class MBEval(ctypes.Structure):
@@ -95,8 +99,9 @@ def lib():
             fn.restype = res
             fn.argtypes = args
         abi = L.mace_b200_abi_version()
-        if abi != 1:
-            raise RuntimeError(f"libmace_b200.so ABI {abi} != 1")
+        if abi != ABI_VERSION:
+            raise RuntimeError(f"libmace_b200.so ABI {abi} != {ABI_VERSION}: rebuild it with "
+                               "`python mace-million_b200/build.py`")
         ms, es = c_i32(), c_i32()
         L.mace_b200_struct_sizes(ctypes.byref(ms), ctypes.byref(es))
         if (ms.value, es.value) != (ctypes.sizeof(MBModel), ctypes.sizeof(MBEval)):

@@ -144,14 +144,47 @@ def fold_weights(model: Mdl.MACEModel, cols) -> dict:
     return out
 
 
+L1_DENSITY_H = 64      # radial-MLP hidden width the density kernels are written for (2 species slots x 64 = C)
+
+
+def l1_density_supported(f: dict) -> bool:
+    """The density-projection layer 1 keeps up to two species slots of 64 hidden features per receiver (K = C)."""
+    return f["S"] <= 2 and f["A0"][3].shape[0] == L1_DENSITY_H
+
+
+def fold_l1_density(f: dict) -> np.ndarray:
+    """Composite layer-1 node matrices of the exact density projection, fp64 [S, 4, 2 H, C]:
+    Kc[s_r, l][slot H + q, c'] = sum_c A3[q, l C + c] X1[slot, c] M0[s_r, l][c, c'] (rows of an absent slot are 0).
+
+    Layer-1 sender features depend only on the sender species and the radial MLP's last layer is linear, so
+    msg1[lm, c] = sum_e W1(r_e)[l, c] X1[s_e, c] Y_lm(e) = sum_{s, q} A3[q, l C + c] X1[s, c] B[s, q, lm] with the
+    per-receiver densities B[s, q, lm] = sum_{e: s_e = s} h_q(r_e) Y_lm(e), h the MLP's last hidden layer
+    (mace_onegpu/ace_layer1.py:2-16 derives it; :60-83 evaluates it).  x1 = msg1 M0[s_r] / (rho1 + 1) is then
+    B Kc[s_r] / (rho1 + 1): the same GEMM shape as the direct path's M0 step (2 H = C = 128)."""
+    A3 = f["A0"][3]                                           # [H, 4 C]
+    H, S = A3.shape[0], f["S"]
+    if 2 * H != C:
+        raise ValueError(f"density layer 1 needs a {C // 2}-wide last hidden layer (got {H})")
+    Kc = np.zeros((S, 4, 2 * H, C))
+    for sr in range(S):
+        for l in range(4):
+            for s in range(S):
+                Kc[sr, l, s * H:(s + 1) * H] = (A3[:, l * C:(l + 1) * C] * f["X1"][s][None, :]) @ f["M0"][sr, l]
+    return Kc
+
+
 class FoldedModel:
     """Device-resident folded model for one species subset (the ctypes mb_model_t points into its tensors)."""
 
     def __init__(self, model: Mdl.MACEModel, cols, spline_grid: int = 512, r_lo: float = 0.5, device="cuda",
-                 use_tc: bool | None = None):
+                 use_tc: bool | None = None, l1_mode: str | None = None):
         L = N.lib()
         if use_tc is None:
             use_tc = os.environ.get("MACE_B200_TC", "1") != "0"
+        if l1_mode is None:
+            l1_mode = os.environ.get("MACE_B200_L1", "auto")
+        if l1_mode not in ("auto", "direct", "density"):
+            raise ValueError(f"l1_mode must be 'auto', 'direct' or 'density' (got {l1_mode!r})")
         self.cols = [int(c) for c in cols]
         self.device = torch.device(device)
         a = model.arch
@@ -166,6 +199,13 @@ class FoldedModel:
                                    "regenerate csrc/symcon_gen.cuh and rebuild")
         S = f["S"]
         self.S = S
+        ok = l1_density_supported(f)
+        if l1_mode == "density" and not ok:
+            raise ValueError("the density-projection layer 1 needs at most 2 species and a 64-wide radial MLP")
+        # layer 1 as per-receiver densities of the MLP's hidden features (exact; one 64-column table) or as direct
+        # per-edge weights W1 * X1 (one 4 C-column table per sender species); auto = density where supported
+        self.l1_density = ok if l1_mode == "auto" else l1_mode == "density"
+        M0 = fold_l1_density(f) if self.l1_density else f["M0"]
         self.M = int(spline_grid)
         self.r_lo = float(r_lo)
         self.r_max = float(a.r_max)
@@ -175,8 +215,8 @@ class FoldedModel:
         t = {}
         t["wd1"] = _f32(f["wd0"], dev)
         t["wd2"] = _f32(f["wd1"], dev)
-        t["M0"] = _f32(f["M0"], dev)
-        t["M0T"] = _f32(np.ascontiguousarray(np.swapaxes(f["M0"], -1, -2)), dev)
+        t["M0"] = _f32(M0, dev)
+        t["M0T"] = _f32(np.ascontiguousarray(np.swapaxes(M0, -1, -2)), dev)
         t["Wp1"] = _f32(f["Wp1"], dev)
         t["Wp1T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wp1"], -1, -2)), dev)
         t["wr0"] = _f32(f["wr0"], dev)
@@ -195,31 +235,38 @@ class FoldedModel:
         t["e0"] = torch.as_tensor(f["e0"], dtype=torch.float64, device=dev).contiguous()
         for name, key, transpose in (("M0", "M0", False), ("Wp1", "Wp1", False), ("Wup2", "Wup2", False),
                                      ("Wsk1", "Wsk1", False), ("Wlin2", "Wlin2", False), ("Wp2", "Wp2", False)):
-            W = f[key]
+            W = M0 if key == "M0" else f[key]
             t[name + "_tc"] = torch.as_tensor(tc_planes(W), device=dev).contiguous()
             t[name + "T_tc"] = torch.as_tensor(tc_planes(np.swapaxes(W, -1, -2)), device=dev).contiguous()
-        # spline tables built on the GPU in fp64 (tab1 carries X1 of the sender species)
+        # spline tables built on the GPU in fp64: tab1 carries X1 of the sender species (direct layer 1) or is the
+        # MLP's last hidden layer h(r) (density layer 1: last-layer matrix = identity, one table for all pairs)
         self.TV, self.TG = {}, {}
         for i, key, D, csk in ((0, "tab1", 4 * C, "col_scale1"), (1, "tab2", 10 * C, None)):
             A = [torch.as_tensor(x, dtype=torch.float64, device=dev).contiguous() for x in f[f"A{i}"]]
             cs = None if csk is None else torch.as_tensor(f[csk], dtype=torch.float64, device=dev).contiguous()
-            TV = torch.empty(S * S, self.M, D, dtype=torch.float32, device=dev)
+            npair = S * S
+            if i == 0 and self.l1_density:
+                D, cs, npair = L1_DENSITY_H, None, 1
+                A[3] = torch.eye(L1_DENSITY_H, dtype=torch.float64, device=dev)
+            TV = torch.empty(npair, self.M, D, dtype=torch.float32, device=dev)
             TG = torch.empty_like(TV)
-            cub = torch.empty(S * S, self.M - 1, D, 4, dtype=torch.float32, device=dev)
+            cub = torch.empty(npair, self.M - 1, D, 4, dtype=torch.float32, device=dev)
             st = torch.cuda.current_stream(dev).cuda_stream
             N.check(L.mace_b200_build_tables(N.ptr(A[0]), N.ptr(A[1]), N.ptr(A[2]), N.ptr(A[3]), A[0].shape[0],
-                                             A[0].shape[1], D, N.ptr(cs), S * S, self.M, self.r_lo, self.r_max,
+                                             A[0].shape[1], D, N.ptr(cs), npair, self.M, self.r_lo, self.r_max,
                                              float(a.num_poly_cutoff), N.ptr(TV), N.ptr(TG), N.ptr(cub), st),
                     "build_tables")
-            cub, tmap = dedup_tables(cub)
-            t[key] = cub
-            t[key + "_map"] = tmap
+            if npair == 1:
+                t[key], t[key + "_map"] = cub, None
+            else:
+                t[key], t[key + "_map"] = dedup_tables(cub)
             self.TV[i], self.TG[i] = TV, TG
             t[f"_A{i}"] = A
         self.t = t
         h = (self.r_max - self.r_lo) / (self.M - 1)
         self.struct = N.MBModel(C=C, S=S, M=self.M, r_lo=self.r_lo, inv_h=1.0 / h, r_max=self.r_max,
                                 p_cut=float(a.num_poly_cutoff), scale=self.scale, use_tc=1 if use_tc else 0,
+                                l1_density=1 if self.l1_density else 0,
                                 **{k: N.ptr(v) for k, v in t.items() if not k.startswith("_")})
         self.use_tc = bool(use_tc)
 
@@ -278,7 +325,7 @@ class ThreePassEngine:
     """The three-pass evaluation on one GPU for a fixed model and species set."""
 
     def __init__(self, model: Mdl.MACEModel, cols, chunk: int = 16384, spline_grid: int = 512, device="cuda",
-                 use_tc: bool | None = None, x1_cache: bool | None = None):
+                 use_tc: bool | None = None, x1_cache: bool | None = None, l1_mode: str | None = None):
         self.device = torch.device(device)
         self.model = model
         self.chunk = int(chunk)
@@ -288,7 +335,7 @@ class ThreePassEngine:
         self.graphs = os.environ.get("MACE_B200_GRAPHS", "0") == "1"
         self._graph = None
         self.captures = 0
-        self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device, use_tc=use_tc)
+        self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device, use_tc=use_tc, l1_mode=l1_mode)
         Zn = len(model.arch.atomic_numbers)
         col2s = torch.full((Zn,), -1, dtype=torch.int64)
         col2s[torch.as_tensor(self.fm.cols)] = torch.arange(len(self.fm.cols))

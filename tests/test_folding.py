@@ -23,11 +23,15 @@ def _silu(z):
     return z / (1.0 + np.exp(-z))
 
 
-def _mlp(A, f):
+def _hidden(A, f):
     h = f
     for W in A[:3]:
         h = _silu(h @ W)
-    return h @ A[3]
+    return h
+
+
+def _mlp(A, f):
+    return _hidden(A, f) @ A[3]
 
 
 def _feats(r, arch):
@@ -51,7 +55,7 @@ def _sc(coef, ents, x, spec, nout_base):
     return out
 
 
-def emulate(f, arch, pi, pj, rij, spec, nl):
+def emulate(f, arch, pi, pj, rij, spec, nl, l1_density=False):
     t1, t2 = M.tp_tables()
     r = np.linalg.norm(rij, axis=1)
     Y = o3.sh_np(3, rij)
@@ -59,17 +63,29 @@ def emulate(f, arch, pi, pj, rij, spec, nl):
     S_ = f["S"]
     ss, sr = spec[pj], spec[pi]
     # layer 1
-    W1 = _mlp(f["A0"], feats).reshape(-1, 4, C) * f["X1"][ss][:, None, :]
     rho1 = np.zeros(nl)
     np.add.at(rho1, pi, np.tanh((feats @ f["wd0"]) ** 2))
-    msg1 = np.zeros((nl, 16, C))
-    for l in range(4):
-        for mm in range(l * l, (l + 1) ** 2):
-            np.add.at(msg1[:, mm, :], pi, W1[:, l, :] * Y[:, mm:mm + 1])
-    x1 = np.zeros_like(msg1)
+    if l1_density:
+        # per-receiver densities B[m][slot H + q] of the MLP's hidden features, then the composite matrices
+        hid = _hidden(f["A0"], feats)                                          # [E, H]
+        H = hid.shape[1]
+        msg1 = np.zeros((nl, 16, 2 * H))
+        for mm in range(16):
+            for s in range(S_):
+                e = ss == s
+                np.add.at(msg1[:, mm, s * H:(s + 1) * H], pi[e], hid[e] * Y[e, mm:mm + 1])
+        M0 = E.fold_l1_density(f)
+    else:
+        W1 = _mlp(f["A0"], feats).reshape(-1, 4, C) * f["X1"][ss][:, None, :]
+        msg1 = np.zeros((nl, 16, C))
+        for l in range(4):
+            for mm in range(l * l, (l + 1) ** 2):
+                np.add.at(msg1[:, mm, :], pi, W1[:, l, :] * Y[:, mm:mm + 1])
+        M0 = f["M0"]
+    x1 = np.zeros((nl, 16, C))
     for l in range(4):
         sl = slice(l * l, (l + 1) ** 2)
-        x1[:, sl, :] = np.einsum("nmc,ncd->nmd", msg1[:, sl, :], f["M0"][spec[:nl], l]) / (rho1[:, None, None] + 1)
+        x1[:, sl, :] = np.einsum("nmc,ncd->nmd", msg1[:, sl, :], M0[spec[:nl], l]) / (rho1[:, None, None] + 1)
     A1 = _sc(f["sc0"], o3.sc_entries((0, 1)), x1, spec[:nl], {0: 0, 1: 1})
     h1 = np.zeros((nl, 4, C))
     h1[:, 0:1] = A1[:, 0:1] @ f["Wp1"][0]
@@ -98,7 +114,10 @@ def emulate(f, arch, pi, pj, rij, spec, nl):
     return f["e0"][spec[:nl]] + arch.scale * (R1 + R2)
 
 
-def test_folded_forward_matches_oracle():
+@pytest.mark.parametrize("l1_density", [False, True], ids=["direct", "density"])
+def test_folded_forward_matches_oracle(l1_density):
+    """Both layer-1 forms: W1 * X1 per edge (direct) and per-receiver hidden-feature densities mapped by the
+    composite matrices of fold_l1_density (exact density projection)."""
     mdl = M.default_model(0)
     pos, Z, box = S.water_box(4, seed=1)
     cols_all = S.species_columns(Z, mdl.arch.atomic_numbers)
@@ -106,10 +125,19 @@ def test_folded_forward_matches_oracle():
     cols = sorted(set(cols_all.tolist()))
     spec = np.array([cols.index(c) for c in cols_all])
     f = E.fold_weights(mdl, cols)
-    e_emu = emulate(f, mdl.arch, pi.numpy().astype(np.int64), pj.numpy().astype(np.int64), rij.numpy(), spec, len(Z))
+    assert E.l1_density_supported(f)
+    e_emu = emulate(f, mdl.arch, pi.numpy().astype(np.int64), pj.numpy().astype(np.int64), rij.numpy(), spec, len(Z),
+                    l1_density=l1_density)
     ref = mace_ref.MaceRef(mdl.params(), dataclasses.asdict(mdl.arch))
     e_ref, _ = ref.three_pass(pi, pj, rij, cols_all, len(Z), 81)
     assert np.abs(e_emu - e_ref.numpy()).max() < 1e-9 * max(1.0, np.abs(e_ref.numpy()).max())
+
+
+def test_density_layer1_needs_at_most_two_species():
+    mdl = M.default_model(1)
+    f = E.fold_weights(mdl, [0, 1, 2])
+    assert not E.l1_density_supported(f)
+    assert E.l1_density_supported(E.fold_weights(mdl, [5]))
 
 
 def test_sc_layout_fingerprint_stable():

@@ -43,18 +43,31 @@ def oracle(mdl, water):
     return dict(ref=ref, eat=eat, pf=pf, H1=H1, G1r=G1r)
 
 
-def _engine(mdl, cols, chunk, use_tc=None):
-    return E.ThreePassEngine(mdl, sorted(set(int(c) for c in cols)), chunk=chunk, device="cuda", use_tc=use_tc)
+def _engine(mdl, cols, chunk, use_tc=None, l1_mode=None):
+    return E.ThreePassEngine(mdl, sorted(set(int(c) for c in cols)), chunk=chunk, device="cuda", use_tc=use_tc,
+                             l1_mode=l1_mode)
 
 
-def test_tables_match_oracle(mdl, water, oracle):
-    eng = _engine(mdl, water["cols"], 64)
+L1_MODES = pytest.mark.parametrize("l1_mode", ["direct", "density"])
+
+
+@L1_MODES
+def test_tables_match_oracle(mdl, water, oracle, l1_mode):
+    eng = _engine(mdl, water["cols"], 64, l1_mode=l1_mode)
+    assert eng.fm.l1_density == (l1_mode == "density")
     ref = oracle["ref"]
     for i in (0, 1):
         tv = eng.fm.TV[i].double().cpu()
         tg = eng.fm.TG[i].double().cpu()
         rt = ref.tables[i]
-        if i == 0:      # layer-1 tables carry X1 of the sender species: compare pair (s, s) against W1 * X1[s]
+        if i == 0 and eng.fm.l1_density:
+            # one table of the MLP's 64 hidden features: mapped through the last layer it gives the oracle's W1
+            A3 = torch.as_tensor(eng.fm.folded["A0"][3])
+            assert tv.shape == (1, 512, 64)
+            want_v, want_g = rt["TV"], rt["TG"]
+            assert (tv[0] @ A3 - want_v).abs().max() <= 2e-6 * want_v.abs().max()
+            assert (tg[0] @ A3 - want_g).abs().max() <= 2e-6 * want_g.abs().max() + 1e-9
+        elif i == 0:    # layer-1 tables carry X1 of the sender species: compare pair (s, s) against W1 * X1[s]
             X1 = torch.as_tensor(eng.fm.folded["X1"])
             S_ = eng.fm.S
             for s in range(S_):
@@ -70,13 +83,15 @@ def test_tables_match_oracle(mdl, water, oracle):
 def test_tables_shared_across_identical_pairs(mdl, water):
     """W2 does not depend on the species pair in this architecture, W1 * X1 only on the sender: water (S = 2) keeps
     one layer-2 and two layer-1 tables, and every pair maps to the right one."""
-    eng = _engine(mdl, water["cols"], 64)
+    eng = _engine(mdl, water["cols"], 64, l1_mode="direct")
     t, S_ = eng.fm.t, eng.fm.S
     assert t["tab2"].shape[0] == 1 and t["tab2_map"].tolist() == [0] * (S_ * S_)
     assert t["tab1"].shape[0] == S_
     m1 = t["tab1_map"].view(S_, S_)
     assert all(len(set(m1[s].tolist())) == 1 for s in range(S_))       # row = sender species
     assert len(set(m1[:, 0].tolist())) == S_
+    dens = _engine(mdl, water["cols"], 64, l1_mode="density").fm.t        # one hidden-feature table, no map
+    assert tuple(dens["tab1"].shape) == (1, 511, 64, 4) and dens["tab1_map"] is None
 
 
 def _run(eng, water, owner=None, nt=None, pj=None):
@@ -103,8 +118,9 @@ def _compare(eat, pf, oracle, water):
     return de, dpf, dF
 
 
-def test_pass_a_h1_matches_oracle(mdl, water, oracle):
-    eng = _engine(mdl, water["cols"], 64)
+@L1_MODES
+def test_pass_a_h1_matches_oracle(mdl, water, oracle, l1_mode):
+    eng = _engine(mdl, water["cols"], 64, l1_mode=l1_mode)
     _run(eng, water)
     H1 = eng._last["H1"].double().cpu()                                  # [n, 4, C]
     want = oracle["H1"].permute(0, 2, 1)
@@ -121,13 +137,30 @@ def test_g1_matches_oracle(mdl, water, oracle):
     assert err <= 2e-5 * want.abs().max().item(), err
 
 
+@L1_MODES
 @pytest.mark.parametrize("use_tc", [True, False], ids=["tcgen05", "simt"])
-def test_energy_and_forces_match_oracle(mdl, water, oracle, use_tc):
-    eng = _engine(mdl, water["cols"], 64, use_tc=use_tc)
+def test_energy_and_forces_match_oracle(mdl, water, oracle, use_tc, l1_mode):
+    eng = _engine(mdl, water["cols"], 64, use_tc=use_tc, l1_mode=l1_mode)
     eat, pf, _ = _run(eng, water)
     de, dpf, dF = _compare(eat, pf, oracle, water)
     assert de < E_TOL and dF < F_TOL and dpf < F_TOL
     assert eng.fmax < 100.0
+
+
+def test_single_species_density_layer1(mdl, water):
+    """One species (S = 1): the density kernels fill only species slot 0 and the composite matrices' slot-1 rows
+    are zero; both layer-1 forms match the oracle."""
+    n = water["n"]
+    o_col = int(S.species_columns(np.array([8]), mdl.arch.atomic_numbers)[0])
+    cols = np.full(n, o_col)
+    ref = mace_ref.MaceRef(mdl.params(), dataclasses.asdict(mdl.arch), spline_knots=512)
+    eat0, pf0 = ref.three_pass(water["pi"], water["pj"], water["rij"], cols, n, 64)
+    for mode in ("density", "direct"):
+        eng = _engine(mdl, cols, 64, l1_mode=mode)
+        assert eng.fm.S == 1 and eng.fm.l1_density == (mode == "density")
+        eat, pf, _ = _run(eng, dict(water, cols=cols))
+        assert (eat - eat0).abs().max() < E_TOL
+        assert (pf - pf0).abs().max() < F_TOL
 
 
 def test_chunk_invariance_gpu(mdl, water):
