@@ -343,8 +343,7 @@ __device__ __forceinline__ int l1d_slot_order(bool ok, int slot, int lane, int& 
   return slot == 1 ? n0 + __popc(m1 & lt) : __popc(m0 & lt);
 }
 
-__device__ __forceinline__ void l1d_accumulate(float (&B)[2][16], const float4* rw, float t, const float* y) {
-  const float h0 = cubic(tab_ld(rw), t), h1 = cubic(tab_ld(rw + 32), t);
+__device__ __forceinline__ void l1d_accumulate(float (&B)[2][16], float h0, float h1, const float* y) {
 #pragma unroll
   for (int k = 0; k < 16; k += 4) {
     const float4 y4 = *reinterpret_cast<const float4*>(y + k);
@@ -395,8 +394,14 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_FWD_MINB) k_edge_l1d_fwd
       rho += ed;
     }
     __syncwarp();
-    for (int q = 0; q < n0; ++q) l1d_accumulate(B0, tab + srow[warp][q], st[warp][q], sY[warp][q]);
-    for (int q = n0; q < nv; ++q) l1d_accumulate(B1, tab + srow[warp][q], st[warp][q], sY[warp][q]);
+    for (int q = 0; q < n0; ++q) {
+      const float4* rw = tab + srow[warp][q];
+      l1d_accumulate(B0, cubic(tab_ld(rw), st[warp][q]), cubic(tab_ld(rw + 32), st[warp][q]), sY[warp][q]);
+    }
+    for (int q = n0; q < nv; ++q) {
+      const float4* rw = tab + srow[warp][q];
+      l1d_accumulate(B1, cubic(tab_ld(rw), st[warp][q]), cubic(tab_ld(rw + 32), st[warp][q]), sY[warp][q]);
+    }
     __syncwarp();
   }
   float* out = ev.s_msg + (size_t)il * 16 * MB_C + lane;
@@ -413,9 +418,9 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_FWD_MINB) k_edge_l1d_fwd
 
 // One edge of the density backward: from g = dE/dB of the edge's species slot, dE/dh_q = sum_m g[q][m] Y_m (into
 // the spline derivative) and this lane's share of dE/dY_m = sum_q g[q][m] h_q, reduced over the warp into sred.
-__device__ __forceinline__ void l1d_edge_bwd(const float (&g)[2][16], const float4* rw, float t, const float* y,
+// c0 / c1: this lane's two coefficient sets of the edge's table row.
+__device__ __forceinline__ void l1d_edge_bwd(const float (&g)[2][16], float4 c0, float4 c1, float t, const float* y,
                                              float* sred_row, int lane) {
-  const float4 c0 = tab_ld(rw), c1 = tab_ld(rw + 32);
   const float h0 = cubic(c0, t), h1 = cubic(c1, t);
   float Y[16];
 #pragma unroll
@@ -501,7 +506,15 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_BWD_MINB) k_edge_l1d_bwd
         g[0][q] = gin[q * MB_C + slot * 64];
         g[1][q] = gin[q * MB_C + slot * 64 + 32];
       }
-      for (int q = q0; q < q1; ++q) l1d_edge_bwd(g, tab + srow[warp][q], st[warp][q], sY[warp][q], sred[warp][q], lane);
+      // the next edge's row is loaded before this edge's work, so its L2 round trip overlaps that work
+      float4 c0 = tab_ld(tab + srow[warp][q0]), c1 = tab_ld(tab + srow[warp][q0] + 32);
+      for (int q = q0; q < q1; ++q) {
+        const int nx = srow[warp][min(q + 1, q1 - 1)];
+        const float4 n0v = tab_ld(tab + nx), n1v = tab_ld(tab + nx + 32);
+        l1d_edge_bwd(g, c0, c1, st[warp][q], sY[warp][q], sred[warp][q], lane);
+        c0 = n0v;
+        c1 = n1v;
+      }
     }
     __syncwarp();
     if (lane < nv) {
