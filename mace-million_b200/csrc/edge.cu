@@ -331,6 +331,7 @@ constexpr int L1D_H = 64;
 #define MB_L1D_BWD_MINB 4
 #endif
 
+
 // Position of this lane's edge in the species-ordered batch (slot 0 first); returns the slot-0 count in n0 and the
 // number of valid edges in nv.  Every lane of the warp calls it.
 __device__ __forceinline__ int l1d_slot_order(bool ok, int slot, int lane, int& n0, int& nv) {
@@ -343,21 +344,30 @@ __device__ __forceinline__ int l1d_slot_order(bool ok, int slot, int lane, int& 
   return slot == 1 ? n0 + __popc(m1 & lt) : __popc(m0 & lt);
 }
 
-__device__ __forceinline__ void l1d_accumulate(float (&B)[2][16], float h0, float h1, const float* y) {
+template <int NH>
+__device__ __forceinline__ void l1d_accumulate(float (&B)[NH][16], const float (&h)[NH], const float* y) {
 #pragma unroll
   for (int k = 0; k < 16; k += 4) {
     const float4 y4 = *reinterpret_cast<const float4*>(y + k);
     const float Y[4] = {y4.x, y4.y, y4.z, y4.w};
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      B[0][k + u] = fmaf(h0, Y[u], B[0][k + u]);
-      B[1][k + u] = fmaf(h1, Y[u], B[1][k + u]);
-    }
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int hh = 0; hh < NH; ++hh) B[hh][k + u] = fmaf(h[hh], Y[u], B[hh][k + u]);
   }
+}
+
+template <int NH>
+__device__ __forceinline__ void l1d_fwd_edge(float (&B)[NH][16], const float4* rw, float t, const float* y) {
+  float h[NH];
+#pragma unroll
+  for (int hh = 0; hh < NH; ++hh) h[hh] = cubic(tab_ld(rw + 32 * hh), t);
+  l1d_accumulate<NH>(B, h, y);
 }
 
 __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_FWD_MINB) k_edge_l1d_fwd(const mb_model_t m, const mb_eval_t ev,
                                                                                 int a, int b) {
+  constexpr int NH = 2;              // blocks of 32 hidden features per lane
   __shared__ __align__(16) float sY[L1_WARPS][32][16];
   __shared__ int srow[L1_WARPS][32];
   __shared__ float st[L1_WARPS][32];
@@ -368,9 +378,11 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_FWD_MINB) k_edge_l1d_fwd
   int64_t e0, e1;
   if (!row_range(ev, i, e0, e1)) return;
   const float4* tab = reinterpret_cast<const float4*>(m.tab1) + lane;
-  float B0[2][16], B1[2][16];        // densities of species slot 0 / 1: [hidden feature lane + 32 hh][m]
+  float B0[NH][16], B1[NH][16];      // densities of species slot 0 / 1: [hidden feature 32 hh + lane][m]
 #pragma unroll
-  for (int q = 0; q < 16; ++q) B0[0][q] = B0[1][q] = B1[0][q] = B1[1][q] = 0.f;
+  for (int q = 0; q < 16; ++q)
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) B0[hh][q] = B1[hh][q] = 0.f;
   float rho = 0.f;
   for (int64_t base = e0; base < e1; base += 32) {
     const int n = (int)min((int64_t)32, e1 - base);
@@ -394,24 +406,18 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_FWD_MINB) k_edge_l1d_fwd
       rho += ed;
     }
     __syncwarp();
-    for (int q = 0; q < n0; ++q) {
-      const float4* rw = tab + srow[warp][q];
-      l1d_accumulate(B0, cubic(tab_ld(rw), st[warp][q]), cubic(tab_ld(rw + 32), st[warp][q]), sY[warp][q]);
-    }
-    for (int q = n0; q < nv; ++q) {
-      const float4* rw = tab + srow[warp][q];
-      l1d_accumulate(B1, cubic(tab_ld(rw), st[warp][q]), cubic(tab_ld(rw + 32), st[warp][q]), sY[warp][q]);
-    }
+    for (int q = 0; q < n0; ++q) l1d_fwd_edge<NH>(B0, tab + srow[warp][q], st[warp][q], sY[warp][q]);
+    for (int q = n0; q < nv; ++q) l1d_fwd_edge<NH>(B1, tab + srow[warp][q], st[warp][q], sY[warp][q]);
     __syncwarp();
   }
   float* out = ev.s_msg + (size_t)il * 16 * MB_C + lane;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    out[q * MB_C] = B0[0][q];
-    out[q * MB_C + 32] = B0[1][q];
-    out[q * MB_C + 64] = B1[0][q];
-    out[q * MB_C + 96] = B1[1][q];
-  }
+  for (int q = 0; q < 16; ++q)
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      out[q * MB_C + 32 * hh] = B0[hh][q];
+      out[q * MB_C + 64 + 32 * hh] = B1[hh][q];
+    }
   rho = warp_sum(rho);
   if (lane == 0) ev.s_rho[il] = rho;
 }
