@@ -759,6 +759,14 @@ __global__ void __launch_bounds__(128, MB_L2_BWD_MINB) k_edge_l2_bwd(const mb_mo
   }
 }
 
+// Edges per batch of the layer-2 kernels (one prologue, main loop and post-pass per batch).
+#ifndef MB_L2F_EB
+#define MB_L2F_EB 64
+#endif
+#ifndef MB_L2B_EB
+#define MB_L2B_EB 64
+#endif
+
 // ------------------------------------------------------------------------------------------------ launchers
 static int edge_args(const mb_model_t* m, const mb_eval_t* ev, int a, int b, const char* who) {
   if (!m || !ev || a < 0 || b > ev->nl || b < a) {
@@ -805,13 +813,13 @@ extern "C" int mace_b200_edge_l1_bwd(const mb_model_t* m, const mb_eval_t* ev, i
 extern "C" int mace_b200_edge_l2_fwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
   if (int rc = edge_args(m, ev, a, b, "edge_l2_fwd")) return rc;
   if (b == a) return 0;
-  k_edge_l2_fwd<64><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  k_edge_l2_fwd<MB_L2F_EB><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
   return check_launch("edge_l2_fwd");
 }
 
 extern "C" int mace_b200_edge_l2_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, int32_t b, void* stream) {
   if (int rc = edge_args(m, ev, a, b, "edge_l2_bwd")) return rc;
   if (b == a) return 0;
-  k_edge_l2_bwd<64><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
+  k_edge_l2_bwd<MB_L2B_EB><<<b - a, 128, 0, (cudaStream_t)stream>>>(*m, *ev, a);
   return check_launch("edge_l2_bwd");
 }
