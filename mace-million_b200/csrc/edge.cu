@@ -547,8 +547,10 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_BWD_MINB) k_edge_l1d_bwd
 
 // ------------------------------------------------------------------------------------------------ layer 2 forward
 // Resident CTAs per SM the layer-2 kernels are compiled for (register budget 65536 / (128 x MINB) per thread).
+// Forward, 1.03M-atom evaluation (128-edge batches): 4 CTAs 111.4 ms, 5: 115.5, 6: 107.2, 7 (72 registers, no
+// spills): 104.9 ms.
 #ifndef MB_L2_FWD_MINB
-#define MB_L2_FWD_MINB 4
+#define MB_L2_FWD_MINB 7
 #endif
 // layer-2 forward: per-edge coefficients by[(w,k,o)] formed by every thread from the 16 SH values (1, default: 60
 // fewer L1 wavefronts per edge and warp for ~80 more FP32 instructions; the kernel is bound by the L1 data path) or
@@ -759,12 +761,15 @@ __global__ void __launch_bounds__(128, MB_L2_BWD_MINB) k_edge_l2_bwd(const mb_mo
   }
 }
 
-// Edges per batch of the layer-2 kernels (one prologue, main loop and post-pass per batch).
+// Edges per batch of the layer-2 kernels (one prologue, main loop and post-pass per batch).  128 covers a water
+// receiver's ~90 edges in one batch, so the prologue and post-pass run on all four warps and once per receiver;
+// measured on the 1.03M-atom evaluation: forward 112.9 -> 110.0 ms, backward 191.7 -> 188.3 ms (32: 114.7 / 195.6).
+// The backward's static shared memory is 47 KB at 128.
 #ifndef MB_L2F_EB
-#define MB_L2F_EB 64
+#define MB_L2F_EB 128
 #endif
 #ifndef MB_L2B_EB
-#define MB_L2B_EB 64
+#define MB_L2B_EB 128
 #endif
 
 // ------------------------------------------------------------------------------------------------ launchers
