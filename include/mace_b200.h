@@ -160,6 +160,9 @@ unsigned long long mace_b200_launch_count(void);
 enum { MB_K_EDGE_L1_FWD = 0, MB_K_EDGE_L1_BWD = 1, MB_K_EDGE_L2_FWD = 2, MB_K_EDGE_L2_BWD = 3, MB_K_SYMCON = 4,
        MB_K_NODE_GEMM = 5, MB_NKINDS = 6 };
 int mace_b200_timing(int enable, double* ms_out, long long* count_out);
+/* Restrict recording to the kinds whose bit (1 << MB_K_*) is set in mask (default: all).  Each recorded launch
+ * costs two event records on its stream, so a caller timing one kernel inside a measured region records only it. */
+int mace_b200_timing_kinds(uint32_t mask);
 /* FP32 FFMA issue ceiling of the current device (TFLOP/s), by an 8-chain FFMA kernel on 8 CTAs per SM (the edge
  * kernels' roofline denominator; scratch is one device float). */
 int mace_b200_ffma_peak(int32_t iters, float* scratch, double* tflops, void* stream);

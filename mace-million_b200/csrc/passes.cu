@@ -24,6 +24,7 @@ static unsigned long long g_launches = 0;       // kernels launched by this libr
 // Optional per-kind CUDA-event timing of the pass runners (enabled by mace_b200_timing(1, ...)).
 struct KindTimer {
   bool on = false;
+  unsigned mask = ~0u;      // kinds recorded while on (bit MB_K_*)
   cudaEvent_t ev[2][8192];
   int kind[8192];
   int n = 0;
@@ -35,7 +36,7 @@ static bool g_tm_init = false;
 
 void timer_begin(int kind, cudaStream_t st, int* slot) {
   *slot = -1;
-  if (!g_tm.on || g_tm.n >= 8192) return;
+  if (!g_tm.on || !((g_tm.mask >> kind) & 1u) || g_tm.n >= 8192) return;
   *slot = g_tm.n++;
   g_tm.kind[*slot] = kind;
   cudaEventRecord(g_tm.ev[0][*slot], st);
@@ -192,6 +193,11 @@ extern "C" int mace_b200_timing(int enable, double* ms_out, long long* count_out
   g_tm.on = enable != 0;
   return 0;
 }
+extern "C" int mace_b200_timing_kinds(uint32_t mask) {
+  g_tm.mask = mask;
+  return 0;
+}
+
 extern "C" const char* mace_b200_last_error(void) { return g_err; }
 
 // The chunk's view of the eval struct: with the layer-1 cache, x1 and rho1 live in the cache rows of the chunk.

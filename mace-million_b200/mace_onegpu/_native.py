@@ -49,6 +49,7 @@ _SIGS = {
     "mace_b200_launch_count": (ctypes.c_ulonglong, []),
     "mace_b200_struct_sizes": (c_i32, [ctypes.POINTER(c_i32), ctypes.POINTER(c_i32)]),
     "mace_b200_timing": (c_i32, [c_i32, c_vp, c_vp]),
+    "mace_b200_timing_kinds": (c_i32, [ctypes.c_uint32]),
     "mace_b200_ffma_peak": (c_i32, [c_i32, c_vp, c_vp, c_vp]),
     "mace_b200_sc_layout": (c_i32, [c_i32, ctypes.POINTER(c_i32), ctypes.POINTER(c_u64)]),
     "mace_b200_build_tables": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_f64, c_f64,
@@ -139,6 +140,12 @@ def timing(enable: bool):
     cnt = (ctypes.c_longlong * len(KINDS))()
     check(lib().mace_b200_timing(1 if enable else 0, ctypes.cast(ms, c_vp), ctypes.cast(cnt, c_vp)), "timing")
     return {k: (ms[i], cnt[i]) for i, k in enumerate(KINDS)}
+
+
+def timing_kinds(kinds=None) -> None:
+    """Record only these kinds (names of KINDS) while timing is on; None = all."""
+    mask = 0xFFFFFFFF if kinds is None else sum(1 << KINDS.index(k) for k in kinds)
+    check(lib().mace_b200_timing_kinds(mask), "timing_kinds")
 
 
 def launch_count() -> int:
