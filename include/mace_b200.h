@@ -51,7 +51,8 @@ typedef struct {
   const float* tab1;           /* [T1][M-1][4][C] float4 cubic coefficients of W1 * X1(sender species), T1 tables;
                                   with l1_density: [M-1][64] float4 cubic coefficients of the radial MLP's last
                                   hidden layer h(r) */
-  const float* tab2;           /* [T2][M-1][10][C] float4 cubic coefficients of W2, T2 tables (see tab*_map) */
+  const float* tab2;           /* [T2][M-1][5][2][C] float4 cubic coefficients of W2, T2 tables (see tab*_map):
+                                  per path pair p, (a, a', b, b') then (c, c', d, d') of paths 2p and 2p + 1 */
   const float* wd1;            /* [8] layer-1 density weights / sqrt(8) */
   const float* wd2;            /* [8] layer-2 density weights / sqrt(8) */
   const float* M0;             /* [S][4][C][C]  linear_1 o skip_tp_1 per species and l; with l1_density the

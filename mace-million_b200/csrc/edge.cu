@@ -552,22 +552,17 @@ __global__ void __launch_bounds__(32 * L1_WARPS, MB_L1D_BWD_MINB) k_edge_l1d_bwd
 #ifndef MB_L2_FWD_MINB
 #define MB_L2_FWD_MINB 7
 #endif
-// layer-2 forward: per-edge coefficients by[(w,k,o)] formed by every thread from the 16 SH values (1, default: 60
-// fewer L1 wavefronts per edge and warp for ~80 more FP32 instructions; the kernel is bound by the L1 data path) or
-// broadcast from shared memory (0).  Measured on the 1.03M-atom evaluation: 112.6 ms (1, 4 CTAs / SM) against
-// 120.6 ms (0, 5 CTAs / SM).
-#ifndef MB_L2F_BYREG
-#define MB_L2F_BYREG 1
-#endif
 #ifndef MB_L2_BWD_MINB
 #define MB_L2_BWD_MINB 4
 #endif
 
-// s_msg[i][o][c] = sum_e sum_(w,k) W2(r_e)[w][c] X2[j_e][k][c] by_e[(w,k,o)];  s_rho[i]
-// by_e[(w,k,o)] = sum_m coef Y_e[m] is formed per thread from Y_e in registers (tp2_fwd_y) by default.
+// s_msg[i][o][c] = sum_e sum_(w,k,m) coef W2(r_e)[w][c] X2[j_e][k][c] Y_e[m];  s_rho[i]
+// The products are formed per thread from Y_e in registers (tp2_fwd_y): keeping the 76 per-edge coefficients
+// sum_m coef Y[m] in shared memory instead costs more L1 wavefronts than the extra FP32 work (125.4 against
+// 107.2 ms at 6 CTAs / SM).
 template <int EB>
 __global__ void __launch_bounds__(128, MB_L2_FWD_MINB) k_edge_l2_fwd(const mb_model_t m, const mb_eval_t ev, int a) {
-  __shared__ __align__(16) float sby[EB][MB_L2F_BYREG ? 16 : TP2_NB_PAD];   // SH values or coefficients by
+  __shared__ __align__(16) float sby[EB][16];   // SH values (the TP coefficients are formed per thread from them)
   __shared__ int srow[EB];
   __shared__ int ssend[EB];
   __shared__ float st[EB];
@@ -599,12 +594,8 @@ __global__ void __launch_bounds__(128, MB_L2_FWD_MINB) k_edge_l2_fwd(const mb_mo
         const float ir = 1.f / r;
         float Y[16];
         sh16<float>(v.x * ir, v.y * ir, v.z * ir, Y);
-#if MB_L2F_BYREG
 #pragma unroll
-        for (int k = 0; k < 16; ++k) sby[c][k] = Y[k];   // the SH values; coefficients are formed per thread
-#else
-        tp2_by(Y, sby[c]);
-#endif
+        for (int k = 0; k < 16; ++k) sby[c][k] = Y[k];
         float ed, ded;
         edge_density(r, m.wd2, x.rd.r_max, x.rd.p, ed, ded);
         rho += ed;
@@ -619,7 +610,6 @@ __global__ void __launch_bounds__(128, MB_L2_FWD_MINB) k_edge_l2_fwd(const mb_mo
       float X[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) X[k] = __ldg(xs + k * MB_C);
-#if MB_L2F_BYREG
       float Y[16];
 #pragma unroll
       for (int k = 0; k < 16; k += 4) {
@@ -627,9 +617,6 @@ __global__ void __launch_bounds__(128, MB_L2_FWD_MINB) k_edge_l2_fwd(const mb_mo
         Y[k] = y4.x; Y[k + 1] = y4.y; Y[k + 2] = y4.z; Y[k + 3] = y4.w;
       }
       tp2_fwd_y(tab + row + c, st[q], X, Y, acc);
-#else
-      tp2_fwd(tab + row + c, st[q], X, sby[q], acc);
-#endif
     }
   }
   float* out = ev.s_msg + (size_t)il * TP2_NO * MB_C + c;

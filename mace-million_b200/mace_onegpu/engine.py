@@ -91,6 +91,18 @@ def dedup_tables(cub: torch.Tensor):
     return cub[reps].contiguous(), tmap
 
 
+def tab2_pair_layout(cub: torch.Tensor) -> torch.Tensor:
+    """Layer-2 cubic tables [T, M-1, nW * C, 4] (column w C + c, coefficients a, b, c, d) -> the paired layout the
+    layer-2 kernels read: per interval [p][half][C] float4 with half 0 = (a_2p, a_2p+1, b_2p, b_2p+1) and
+    half 1 = (c_2p, c_2p+1, d_2p, d_2p+1), so that paths 2p and 2p + 1 are evaluated with packed FP32x2 FMAs.
+    Same size, same row offset per interval."""
+    T, K, D, four = cub.shape
+    nW = D // C
+    assert four == 4 and D == nW * C and nW % 2 == 0
+    x = cub.view(T, K, nW // 2, 2, C, 2, 2)                  # [t, k, p, path in pair, c, h, j]: coefficient 2 h + j
+    return x.permute(0, 1, 2, 5, 4, 6, 3).contiguous().view(T, K, D, 4)
+
+
 def fold_weights(model: Mdl.MACEModel, cols) -> dict:
     """All folded fp64 arrays (CPU numpy) for the species columns `cols` (model one-hot columns present)."""
     a = model.arch
@@ -260,6 +272,8 @@ class FoldedModel:
                 t[key], t[key + "_map"] = cub, None
             else:
                 t[key], t[key + "_map"] = dedup_tables(cub)
+            if key == "tab2":
+                t[key] = tab2_pair_layout(t[key])
             self.TV[i], self.TG[i] = TV, TG
             t[f"_A{i}"] = A
         self.t = t

@@ -170,3 +170,19 @@ def test_dedup_tables_merges_only_identical():
     assert t.shape[0] == 4
     for p in range(cub.shape[0]):
         assert torch.equal(t[m[p]], cub[p])
+
+
+def test_tab2_pair_layout_is_the_documented_permutation():
+    """[p][half][C] float4: half 0 = (a_2p, a_2p+1, b_2p, b_2p+1), half 1 = (c_2p, c_2p+1, d_2p, d_2p+1)."""
+    T, K, nW = 2, 3, 10
+    cub = torch.randn(T, K, nW * C, 4)
+    out = E.tab2_pair_layout(cub)
+    assert out.shape == cub.shape
+    o = out.view(T, K, nW // 2, 2, C, 4)
+    src = cub.view(T, K, nW, C, 4)
+    for p in range(nW // 2):
+        w0, w1 = 2 * p, 2 * p + 1
+        assert torch.equal(o[:, :, p, 0], torch.stack([src[:, :, w0, :, 0], src[:, :, w1, :, 0],
+                                                       src[:, :, w0, :, 1], src[:, :, w1, :, 1]], -1))
+        assert torch.equal(o[:, :, p, 1], torch.stack([src[:, :, w0, :, 2], src[:, :, w1, :, 2],
+                                                       src[:, :, w0, :, 3], src[:, :, w1, :, 3]], -1))
