@@ -170,6 +170,22 @@ __device__ __forceinline__ void spline_coords(float r, const Radial& rd, int& k,
   t = x - kf;
 }
 
+// Warp-wide sums of 16 per-lane values with 16 shuffles: each step exchanges half of the remaining values with the
+// partner lane of one bit, so that lane L ends with the sum over the warp of v[L >> 1].
+__device__ __forceinline__ float transpose_reduce16(float* v, int lane) {
+#pragma unroll
+  for (int h = 8, bit = 16; h >= 1; h >>= 1, bit >>= 1) {
+    const bool up = lane & bit;
+#pragma unroll
+    for (int q = 0; q < h; ++q) {
+      const float send = up ? v[q] : v[q + h];
+      const float keep = up ? v[q + h] : v[q];
+      v[q] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
 }  // namespace mb
 
 // ---------------------------------------------------------------------------------------------- error plumbing

@@ -86,7 +86,6 @@ __device__ __forceinline__ void sh_jacobian(float3 u, float r, float* Y, float* 
 }
 
 __device__ __forceinline__ float cubic(float4 q, float t) { return fmaf(fmaf(fmaf(q.w, t, q.z), t, q.y), t, q.x); }
-__device__ __forceinline__ float dcubic(float4 q, float t) { return fmaf(fmaf(3.f * q.w, t, 2.f * q.z), t, q.y); }
 
 __device__ __forceinline__ float block_sum128(float v, float* red4) {
   v = warp_sum(v);
@@ -94,22 +93,6 @@ __device__ __forceinline__ float block_sum128(float v, float* red4) {
   if ((threadIdx.x & 31) == 0) red4[threadIdx.x >> 5] = v;
   __syncthreads();
   return red4[0] + red4[1] + red4[2] + red4[3];
-}
-
-// Warp-wide sums of 16 per-lane values with 16 shuffles: each step exchanges half of the remaining values with the
-// partner lane of one bit, so that lane L ends with the sum over the warp of v[L >> 1].
-__device__ __forceinline__ float transpose_reduce16(float* v, int lane) {
-#pragma unroll
-  for (int h = 8, bit = 16; h >= 1; h >>= 1, bit >>= 1) {
-    const bool up = lane & bit;
-#pragma unroll
-    for (int q = 0; q < h; ++q) {
-      const float send = up ? v[q] : v[q + h];
-      const float keep = up ? v[q + h] : v[q];
-      v[q] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
-    }
-  }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
 // ------------------------------------------------------------------------------------------------ layer 1

@@ -220,20 +220,6 @@ __global__ void __launch_bounds__(128) k_symcon_bwd(const float* __restrict__ co
 // One warp per atom (grid-stride), lane channels c = lane + 32 jj; W1r [128][16] stays in registers (64 per lane)
 // across the warp's atoms.  z_j = sum_c h_c W1r[c][j] is reduced over the warp with a 16-value transpose reduction
 // (lane L ends with z_{L >> 1}); e = sum_j silu(z_j) w2r_j;  g_h2[c] = scale sum_j W1r[c][j] w2r_j silu'(z_j).
-__device__ __forceinline__ float readout_tr16(float* v, int lane) {
-#pragma unroll
-  for (int h = 8, bit = 16; h >= 1; h >>= 1, bit >>= 1) {
-    const bool up = lane & bit;
-#pragma unroll
-    for (int q = 0; q < h; ++q) {
-      const float send = up ? v[q] : v[q + h];
-      const float keep = up ? v[q + h] : v[q];
-      v[q] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
-    }
-  }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
-}
-
 __global__ void __launch_bounds__(256) k_readout2(const float* __restrict__ h2, const float* __restrict__ W1r,
                                                   const float* __restrict__ w2r, float scale, double* __restrict__ eat,
                                                   float* __restrict__ gh2, int n) {
@@ -259,7 +245,7 @@ __global__ void __launch_bounds__(256) k_readout2(const float* __restrict__ h2, 
       for (int jj = 1; jj < 4; ++jj) t = fmaf(h[jj], w[jj][j], t);
       z[j] = t;
     }
-    const float zj = readout_tr16(z, lane);
+    const float zj = transpose_reduce16(z, lane);
     const float sig = 1.f / (1.f + expf(-zj));
     float e = (lane & 1) ? 0.f : zj * sig * w2;  // one lane of each pair
     const float sg = scale * w2 * sig * (1.f + zj * (1.f - sig));
