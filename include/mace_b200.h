@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define MB_ABI_VERSION 2
+#define MB_ABI_VERSION 3
 
 enum {
   MB_OK = 0,
