@@ -56,7 +56,7 @@ FLOPS_PER_EDGE_L1D = {"edge_l1_fwd": 8 * 64 + 2 * 64 * 16, "edge_l1_bwd": 8 * 64
 # DRAM traffic of one launch of the dominant kernel, from a one-pass ncu capture of this bench's own command
 # (`ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:k_edge_l2_bwd -s 10 -c 1 python bench.py
 # --steps 1 --warmup 1 --no-e2e --no-cpu-baseline`): a 16,384-receiver chunk of the 1.03M-atom water box.
-TRAFFIC_PER_LAUNCH = {("water_1m", 16384, "edge_l2_bwd"): 738.88e6 + 167.27e6}
+TRAFFIC_PER_LAUNCH = {("water_1m", 16384, "edge_l2_bwd"): 703.40e6 + 149.40e6}
 EDGE_PASSES = {"edge_l1_fwd": 1, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
 
 
