@@ -1,14 +1,15 @@
-"""Full neighbour list (both directions) of an orthorhombic periodic box: cell list + minimum image, in torch so that
-it runs on the host or on the GPU (input preparation for the standalone driver; the force evaluation itself takes the
-pair list as given, like the ML-IAP boundary).  The algorithm is the one of the reference's
-``System.build_neighbors`` (``mace_onegpu/receiver_chunk_mace.py:114-165``): 27-cell candidates per atom, a count
-pass then a fill pass, brute force when a box dimension holds fewer than 3 cells.
+"""Full neighbour list (both directions) of an orthorhombic periodic box or of an open point set with explicit ghost
+images (input preparation for the standalone driver; the force evaluation itself takes the pair list as given, like
+the ML-IAP boundary; the reference builds its standalone list in ``System.build_neighbors``,
+``mace_onegpu/receiver_chunk_mace.py:114-165``).
 
 Output convention: pairs sorted by receiver i, rij = x_i - x_j (minimum image), the edge vector of mace's
 ``get_edge_vectors_and_lengths`` (receiver minus sender).  On a CUDA device (and at least 3 cells per periodic
 dimension) the lists come from the library's cell-list kernels (mace_b200_nbr_count / _fill, one warp per receiver,
-senders of a receiver in a fixed cell-scan order); on the host the torch version below sorts senders by index.
-``verlet_filter`` reduces a skin list to the pairs within the cutoff at new positions (mace_b200_verlet_filter).
+senders of a receiver in a fixed cell-scan order).  On the host a k-d tree (scipy's cKDTree, periodic via its
+``boxsize``) finds the unordered pairs, which are mirrored and sorted by (receiver, sender); it is the checker of
+the CUDA lists in the tests.  ``verlet_filter`` reduces a skin list to the pairs within the cutoff at new positions
+(mace_b200_verlet_filter).
 """
 from __future__ import annotations
 
@@ -87,104 +88,65 @@ def verlet_filter(pos, box, vrow, vj, r_cut: float):
     return pi, pj, rij
 
 
-def neighbor_list(pos, box, r_max: float, device="cpu", block: int = 16384, return_rowptr: bool = False):
+def _host_pairs(pos, n_recv: int, r_max: float, box=None, return_rowptr: bool = False):
+    """Host pair search with a k-d tree (scipy's cKDTree; periodic when `box` is given, which needs every box
+    length > 2 r_max so that each pair has exactly one image).  pos / box: fp64 CPU tensors.  Returns (pi int32,
+    pj int32, rij fp64 = x_i - x_j[, rowptr int64 [n_recv + 1]]) for receivers i < n_recv and every sender j != i
+    with |x_i - x_j| < r_max, sorted by (i, j)."""
+    from scipy.spatial import cKDTree
+
+    pos_np = pos.numpy()
+    tree = cKDTree(pos_np, boxsize=box.numpy()) if box is not None else cKDTree(pos_np)
+    ij = torch.from_numpy(tree.query_pairs(r_max, output_type="ndarray")).long()   # a < b, |d| <= r_max
+    pi = torch.cat([ij[:, 0], ij[:, 1]])
+    pj = torch.cat([ij[:, 1], ij[:, 0]])
+    keep = pi < n_recv
+    pi, pj = pi[keep], pj[keep]
+    d = pos[pi] - pos[pj]
+    if box is not None:
+        d -= box * torch.round(d / box)
+    strict = (d * d).sum(-1) < r_max * r_max                               # the kernels' strict cutoff
+    pi, pj, d = pi[strict], pj[strict], d[strict]
+    o = torch.argsort(pi * pos.shape[0] + pj)
+    pi, pj, d = pi[o], pj[o], d[o].contiguous()
+    out = (pi.to(torch.int32), pj.to(torch.int32), d)
+    if return_rowptr:
+        rp = torch.zeros(n_recv + 1, dtype=torch.int64)
+        rp[1:] = torch.cumsum(torch.bincount(pi, minlength=n_recv), 0)
+        out = out + (rp,)
+    return out
+
+
+def neighbor_list(pos, box, r_max: float, device="cpu", return_rowptr: bool = False):
     """Returns (pi int32 [P], pj int32 [P], rij float64 [P, 3]) for all 0 < |x_i - x_j|_mic < r_max (and the receiver
-    row pointer int64 [N + 1] with return_rowptr)."""
+    row pointer int64 [N + 1] with return_rowptr).  CUDA device: the library's cell-list kernels; host: a periodic
+    k-d tree, pairs sorted by (i, j)."""
     pos = torch.as_tensor(pos, dtype=torch.float64, device=device)
     box = torch.as_tensor(box, dtype=torch.float64, device=device)
     if not bool((box > 2.0 * r_max).all()):
         raise ValueError("minimum image needs every box length > 2 r_max")
     pos = torch.remainder(pos, box).contiguous()
     N = pos.shape[0]
-    r2 = r_max * r_max
     nc = torch.clamp((box / r_max).floor().long(), min=1)
-    brute = bool((nc < 3).any())
-    if pos.is_cuda and not brute:
+    if pos.is_cuda and not bool((nc < 3).any()):
         zero = torch.zeros(3, dtype=torch.float64, device=pos.device)
         return _cuda_pairs(pos, N, zero, box / nc, nc, box, True, r_max, return_rowptr)
-    if not brute:
-        c = torch.minimum((pos / (box / nc)).floor().long(), nc - 1)
-        lin = (c[:, 0] * nc[1] + c[:, 1]) * nc[2] + c[:, 2]
-        order = torch.argsort(lin, stable=True)
-        lin_sorted = lin[order]
-        ncell = int(nc.prod())
-        counts = torch.bincount(lin_sorted, minlength=ncell)
-        start = torch.cumsum(counts, 0) - counts
-        mcc = int(counts.max())
-        offs = torch.stack(torch.meshgrid(*[torch.arange(-1, 2, device=device)] * 3, indexing="ij"), -1).reshape(27, 3)
-    out_i, out_j = [], []
-    for a in range(0, N, block):
-        b = min(a + block, N)
-        ri = torch.arange(a, b, device=device)
-        if brute:
-            cand = torch.arange(N, device=device).unsqueeze(0).expand(b - a, N)
-            valid = torch.ones_like(cand, dtype=torch.bool)
-        else:
-            cc = (c[a:b].unsqueeze(1) + offs.unsqueeze(0)) % nc
-            cl = (cc[..., 0] * nc[1] + cc[..., 1]) * nc[2] + cc[..., 2]
-            k = torch.arange(mcc, device=device)
-            slot = start[cl].unsqueeze(-1) + k
-            valid = (k < counts[cl].unsqueeze(-1)).reshape(b - a, -1)
-            cand = order[torch.where(valid, slot.reshape(b - a, -1), torch.zeros_like(valid, dtype=torch.long))]
-        d = pos[ri].unsqueeze(1) - pos[cand]
-        d = d - box * torch.round(d / box)
-        ok = valid & ((d * d).sum(-1) < r2) & (cand != ri.unsqueeze(1))
-        ii, kk = ok.nonzero(as_tuple=True)
-        out_i.append(ii + a)
-        out_j.append(cand[ii, kk])
-    pi = torch.cat(out_i)
-    pj = torch.cat(out_j)
-    key = pi * N + pj
-    o = torch.argsort(key)
-    pi, pj = pi[o], pj[o]
-    rij = pos[pi] - pos[pj]
-    rij = rij - box * torch.round(rij / box)
-    if return_rowptr:
-        rowptr = torch.searchsorted(pi, torch.arange(N + 1, device=pi.device))
-        return pi.to(torch.int32), pj.to(torch.int32), rij, rowptr
-    return pi.to(torch.int32), pj.to(torch.int32), rij
+    pos, box = pos.cpu(), box.cpu()
+    # cKDTree's periodic domain is [0, L); torch.remainder can round a tiny negative coordinate up to exactly L
+    pos = torch.where(pos >= box, pos - box, pos)
+    return tuple(t.to(device) for t in _host_pairs(pos, N, r_max, box, return_rowptr))
 
 
-def neighbor_list_open(pos, n_recv: int, r_max: float, device="cpu", block: int = 16384):
+def neighbor_list_open(pos, n_recv: int, r_max: float, device="cpu"):
     """Pairs of an open (non-periodic) point set with explicit ghost images: receivers are atoms [0, n_recv),
-    senders any atom, 0 < |x_i - x_j| < r_max.  Cell list over the bounding box (cells >= r_max, 27 neighbours
-    without wrap).  Returns (pi int32, pj int32, rij fp64 = x_i - x_j) sorted by (pi, pj)."""
+    senders any atom, 0 < |x_i - x_j| < r_max.  CUDA device: the cell-list kernels over the bounding box (cells
+    >= r_max, 27 neighbours without wrap); host: a k-d tree.  Returns (pi int32, pj int32, rij fp64 = x_i - x_j)
+    sorted by (pi, pj)."""
     pos = torch.as_tensor(pos, dtype=torch.float64, device=device).contiguous()
-    N = pos.shape[0]
-    lo = pos.min(0).values
-    ext = pos.max(0).values - lo
-    nc = torch.clamp((ext / r_max).floor().long(), min=1)
     if pos.is_cuda:
+        lo = pos.min(0).values
+        ext = pos.max(0).values - lo
+        nc = torch.clamp((ext / r_max).floor().long(), min=1)
         width = torch.maximum(ext / nc, torch.full_like(ext, r_max))
         return _cuda_pairs(pos, n_recv, lo, width, nc, lo, False, r_max)
-    c = torch.minimum(((pos - lo) / (ext / nc + 1e-12)).floor().long(), nc - 1)
-    lin = (c[:, 0] * nc[1] + c[:, 1]) * nc[2] + c[:, 2]
-    order = torch.argsort(lin, stable=True)
-    ncell = int(nc.prod())
-    counts = torch.bincount(lin, minlength=ncell)
-    start = torch.cumsum(counts, 0) - counts
-    mcc = int(counts.max())
-    offs = torch.stack(torch.meshgrid(*[torch.arange(-1, 2, device=device)] * 3, indexing="ij"), -1).reshape(27, 3)
-    r2 = r_max * r_max
-    out_i, out_j = [], []
-    for a in range(0, n_recv, block):
-        b = min(a + block, n_recv)
-        ri = torch.arange(a, b, device=device)
-        cc = c[a:b].unsqueeze(1) + offs.unsqueeze(0)                          # [n, 27, 3]
-        inb = ((cc >= 0) & (cc < nc)).all(-1)
-        cc = torch.where(inb.unsqueeze(-1), cc, torch.zeros_like(cc))
-        cl = (cc[..., 0] * nc[1] + cc[..., 1]) * nc[2] + cc[..., 2]
-        k = torch.arange(mcc, device=device)
-        slot = start[cl].unsqueeze(-1) + k
-        valid = ((k < counts[cl].unsqueeze(-1)) & inb.unsqueeze(-1)).reshape(b - a, -1)
-        cand = order[torch.where(valid, slot.reshape(b - a, -1), torch.zeros_like(valid, dtype=torch.long))]
-        d = pos[ri].unsqueeze(1) - pos[cand]
-        ok = valid & ((d * d).sum(-1) < r2) & (cand != ri.unsqueeze(1))
-        ii, kk = ok.nonzero(as_tuple=True)
-        out_i.append(ii + a)
-        out_j.append(cand[ii, kk])
-    pi = torch.cat(out_i)
-    pj = torch.cat(out_j)
-    o = torch.argsort(pi * N + pj)
-    pi, pj = pi[o], pj[o]
-    return pi.to(torch.int32), pj.to(torch.int32), pos[pi] - pos[pj]
+    return _host_pairs(pos, n_recv, r_max)
