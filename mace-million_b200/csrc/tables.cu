@@ -118,14 +118,8 @@ extern "C" int mace_b200_build_tables(const double* A0, const double* A1, const 
 // as mace_b200_build_tables, but its fp64 sample scratch is this file-scope device array instead of a
 // cudaMallocAsync buffer.  Capacity: M * D <= 512 * 1280 (the largest table of the MACE-MPA-0 architecture at the
 // default 512-knot grid), i.e. 3 * 655,360 doubles = 15 MiB, held by every GPU that loads the library until exit.
-#include <mutex>
-
 static constexpr size_t kNoAllocMD = 512 * 1280;
 static __device__ __align__(256) double g_noalloc_samples[3 * kNoAllocMD];
-
-static std::mutex g_noalloc_mu;
-static constexpr int kMaxDevices = 64;
-static double* g_noalloc_ptr[kMaxDevices] = {nullptr};   // device address of g_noalloc_samples, per device ordinal
 
 extern "C" int mace_b200_build_tables_noalloc(const double* A0, const double* A1, const double* A2, const double* A3,
                                               int32_t n_in, int32_t hidden, int32_t D, const double* col_scale,
@@ -141,25 +135,13 @@ extern "C" int mace_b200_build_tables_noalloc(const double* A0, const double* A1
               "columns); use mace_b200_build_tables", (long long)M * D, kNoAllocMD);
     return MB_E_ARG;
   }
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    set_error("build_tables_noalloc: no usable current device");
-    return MB_E_CUDA;
-  }
+  // The symbol is only a host-side stand-in: resolve the scratch's device address on the current device (every call;
+  // cudaGetSymbolAddress is cheap and no stream operation, and nothing cached goes stale after a device reset).
   double* smp = nullptr;
-  {
-    // first call on this device: resolve the device address of the static scratch (the symbol itself is only a
-    // host-side stand-in); host code must never hand the symbol to a kernel.
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      cudaError_t e = cudaGetSymbolAddress((void**)&g_noalloc_ptr[dev], g_noalloc_samples);
-      if (e != cudaSuccess) {
-        g_noalloc_ptr[dev] = nullptr;
-        set_error("build_tables_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-        return MB_E_CUDA;
-      }
-    }
-    smp = g_noalloc_ptr[dev];
+  cudaError_t e = cudaGetSymbolAddress((void**)&smp, g_noalloc_samples);
+  if (e != cudaSuccess || !smp) {
+    set_error("build_tables_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    return MB_E_CUDA;
   }
   cudaStream_t st = (cudaStream_t)stream;
   const double h = (r_max - r_lo) / (M - 1);

@@ -61,9 +61,8 @@ def test_noalloc_rejects_tables_beyond_its_capacity():
     L = N.lib()
     mdl, A, cs, D, P, _ = _inputs(1)
     st = torch.cuda.current_stream().cuda_stream
-    out = torch.empty(16, dtype=torch.float32, device="cuda")
+    # null outputs: even if the capacity check stopped firing, the kernels skip null TV / TG / cubic (nothing written)
     rc = L.mace_b200_build_tables_noalloc(N.ptr(A[0]), N.ptr(A[1]), N.ptr(A[2]), N.ptr(A[3]), A[0].shape[0],
-                                          A[0].shape[1], D, None, P, 1024, 0.5, 6.0, 5.0, N.ptr(out), N.ptr(out),
-                                          N.ptr(out), st)
+                                          A[0].shape[1], D, None, P, 1024, 0.5, 6.0, 5.0, None, None, None, st)
     assert rc != 0
     assert b"capacity" in ctypes.string_at(L.mace_b200_last_error())
