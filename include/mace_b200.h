@@ -40,6 +40,7 @@ enum {
   MB_ST_NONFINITE = 8,
   MB_ST_BAD_RECEIVER = 16,
   MB_ST_TC_TIMEOUT = 32,      /* a tensor-core kernel gave up waiting on its MMA barrier (bounded wait) */
+  MB_ST_UNSORTED = 64,        /* mace_b200_csr_rows: pair_i not receiver-sorted inside a chunk */
 };
 
 /* Folded, device-resident model (fp32 unless noted).  S = number of species present (compact indices),
@@ -187,9 +188,10 @@ int mace_b200_build_tables(const double* A0, const double* A1, const double* A2,
  * have the library allocate device memory (an MD engine that owns all device memory through its own pool, or a
  * process with a fixed device footprint): same arguments and outputs, but the fp64 sample scratch is a static device
  * array of the library, so M * D is limited to 512 * 1280 (15 MiB, held by every GPU that loads the library until
- * exit); larger tables are rejected with MB_E_ARG.  It calls no cudaMalloc / cudaFree.  The first call on a device
- * resolves the scratch's device address (cudaGetSymbolAddress) with that device current: make that first call
- * before any stream capture.  All calls share the scratch, so calls that overlap on the GPU race: serialise them. */
+ * exit); larger tables are rejected with MB_E_ARG.  It calls no cudaMalloc / cudaFree.  Every call resolves the
+ * scratch's device address (cudaGetSymbolAddress) on the current device, so the first call on a device (which loads
+ * the module there) should come before any stream capture.  All calls share the scratch, so calls that overlap on the
+ * GPU race: serialise them. */
 int mace_b200_build_tables_noalloc(const double* A0, const double* A1, const double* A2, const double* A3,
                                    int32_t n_in, int32_t hidden, int32_t D, const double* col_scale, int32_t n_pairs,
                                    int32_t M, double r_lo, double r_max, double p_cut, float* TV, float* TG,
@@ -297,6 +299,14 @@ int mace_b200_verlet_filter(const double* pos, const double* box, int32_t period
                             const int64_t* vrow, const int32_t* vj, double r_cut, int32_t* counts,
                             const int64_t* rowptr, int32_t* pi, int32_t* pj, double* rij, uint32_t* status,
                             void* stream);
+
+/* ---------------------------------------------------------------- chunk-wise CSR (streamed pair lists)
+ * Replaces the receiver CSR of mliap_threepass.py:468-478 (searchsorted over the whole pair_i on the device) for a
+ * pair list that arrives chunk by chunk: rowptr[i] for i = a .. b from the chunk's edges [e0, e1) of a
+ * receiver-sorted pair_i (first e with pair_i[e] >= i, e1 if none); an edge of the chunk whose receiver is outside
+ * [a, b) or below its predecessor's sets MB_ST_UNSORTED in *status (the caller then sorts and evaluates again). */
+int mace_b200_csr_rows(const int32_t* pair_i, int64_t e0, int64_t e1, int32_t a, int32_t b, int32_t* rowptr,
+                       uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

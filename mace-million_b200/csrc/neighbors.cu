@@ -232,3 +232,44 @@ extern "C" int mace_b200_verlet_filter(const double* pos, const double* box, int
                                                                                  rowptr, pi, pj, rij, status);
   return check_launch("verlet_filter");
 }
+
+// ------------------------------------------------------------------------------------------------ CSR rows
+// Row pointer of one receiver chunk [a, b) of a receiver-sorted pair list whose edges of the chunk are [e0, e1):
+// rowptr[i] = first e in [e0, e1) with pair_i[e] >= i (e1 if none), i = a .. b.  It lets the host stream the pair
+// list to the device chunk by chunk (the chunks' edge ranges come from a host binary search of the pinned pair_i)
+// and verifies the sortedness that search assumed: an edge whose receiver lies outside [a, b) or below its
+// predecessor's sets MB_ST_UNSORTED, and the host then evaluates again from a sorted copy.
+namespace mb {
+__global__ void k_csr_rows(const int32_t* __restrict__ pi, int64_t e0, int64_t e1, int a, int b,
+                           int32_t* __restrict__ rowptr, unsigned* __restrict__ status) {
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t q = t0; q <= (int64_t)(b - a); q += stride) {
+    const int i = a + (int)q;
+    int64_t lo = e0, hi = e1;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (__ldg(pi + mid) < i) lo = mid + 1;
+      else hi = mid;
+    }
+    rowptr[i] = (int32_t)lo;
+  }
+  bool bad = false;
+  for (int64_t e = e0 + t0; e < e1; e += stride) {
+    const int p = __ldg(pi + e);
+    bad |= p < a || p >= b || (e > e0 && p < __ldg(pi + e - 1));
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_status(status, MB_ST_UNSORTED);
+}
+}  // namespace mb
+
+extern "C" int mace_b200_csr_rows(const int32_t* pair_i, int64_t e0, int64_t e1, int32_t a, int32_t b,
+                                  int32_t* rowptr, uint32_t* status, void* stream) {
+  if (!pair_i || !rowptr || !status || e0 < 0 || e1 < e0 || e1 > INT32_MAX || a < 0 || b < a) {
+    set_error("csr_rows: bad arguments (edges [%lld, %lld), receivers [%d, %d))", (long long)e0, (long long)e1, a, b);
+    return MB_E_ARG;
+  }
+  const int64_t work = (e1 - e0) > (int64_t)(b - a) + 1 ? (e1 - e0) : (int64_t)(b - a) + 1;
+  const int64_t blocks = (work + 255) / 256 < 1184 ? (work + 255) / 256 : 1184;
+  k_csr_rows<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(pair_i, e0, e1, a, b, rowptr, status);
+  return check_launch("csr_rows");
+}

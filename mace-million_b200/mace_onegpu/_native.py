@@ -17,6 +17,7 @@ c_vp = ctypes.c_void_p
 
 
 ABI_VERSION = 3          # MB_ABI_VERSION of include/mace_b200.h this binding mirrors
+ST_UNSORTED = 64         # MB_ST_UNSORTED
 
 
 class MBModel(ctypes.Structure):
@@ -82,6 +83,7 @@ _SIGS = {
                                    c_vp, c_vp, c_vp]),
     "mace_b200_verlet_filter": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_f64, c_vp, c_vp, c_vp, c_vp, c_vp,
                                         c_vp, c_vp]),
+    "mace_b200_csr_rows": (c_i32, [c_vp, c_i64, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp]),
 }
 
 _lib = None

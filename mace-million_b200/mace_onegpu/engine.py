@@ -286,53 +286,79 @@ class FoldedModel:
 
 
 class Plan:
-    """Per-call preparation: receiver-sorted pairs, CSR, compact species, species-sorted chunk order."""
+    """Per-call preparation: receiver-sorted pairs, CSR, compact species, species-sorted chunk order.
 
-    def __init__(self, eng: "ThreePassEngine", pair_i, pair_j, rij, elems, nl: int, nt: int):
+    Pinned host pair arrays (pair_i / pair_j int32, rij fp64, contiguous) that look receiver-sorted stay on the host:
+    the chunks' edge ranges come from a binary search of the pinned pair_i, and the evaluation streams every chunk's
+    pairs to the device on a side stream, where mace_b200_csr_rows forms the chunk's rows and checks the
+    sortedness the search assumed (host_src).  Anything else is copied here, sorted by receiver when needed
+    (stable, like the reference's argsort, mliap_threepass.py:472-474) and its CSR formed on the device."""
+
+    def __init__(self, eng: "ThreePassEngine", pair_i, pair_j, rij, elems, nl: int, nt: int, stream_host: bool = True):
         dev = eng.device
-        pi = torch.as_tensor(pair_i, device=dev).to(torch.int32)
-        self.P = int(pi.numel())
+        self.nl, self.nt = int(nl), int(nt)
+        self.P = int(pair_i.shape[0])
         self.perm = None
-        ordered = self.P <= 1 or bool((pi[1:] >= pi[:-1]).all())
-        # receiver-sorted pairs whose senders / vectors are still in pinned host memory: the evaluation copies them
-        # chunk by chunk on a side stream while pass A runs (host_src); otherwise they are copied (and sorted) here
         self.host_src = None
-        pjh, rh = pair_j, rij
-        if (ordered and isinstance(pjh, torch.Tensor) and isinstance(rh, torch.Tensor) and not pjh.is_cuda
-                and not rh.is_cuda and pjh.is_pinned() and rh.is_pinned() and pjh.dtype == torch.int32
-                and rh.dtype == torch.float64 and pjh.is_contiguous() and rh.is_contiguous()):
-            self.host_src = (pjh.view(-1), rh.view(-1, 3))
-            pj = torch.empty(self.P, dtype=torch.int32, device=dev)
-            rij = torch.empty(self.P, 3, dtype=torch.float64, device=dev)
+        self._inputs = (pair_i, pair_j, rij, elems)
+        C_ = eng.chunk
+        nch = (self.nl + C_ - 1) // C_
+        self.n_chunks = nch
+        bounds = torch.clamp(torch.arange(nch + 1, dtype=torch.int64) * C_, max=self.nl)
+        e_off = None
+        if stream_host and self.P > 1 and nch > 0 and _pinned(pair_i, torch.int32) and \
+                _pinned(pair_j, torch.int32) and _pinned(rij, torch.float64):
+            hpi = pair_i.view(-1)
+            e_off = torch.searchsorted(hpi, bounds.to(torch.int32)).numpy().astype(np.int64)
+            if e_off[0] != 0 or e_off[-1] != self.P or bool((np.diff(e_off) < 0).any()):
+                e_off = None                   # not receiver-sorted (or receivers outside [0, nl)): copy and sort
+        if e_off is not None:
+            self.host_src = (hpi, pair_j.view(-1), rij.view(-1, 3))
+            self.pi = torch.empty(self.P, dtype=torch.int32, device=dev)
+            self.pj = torch.empty(self.P, dtype=torch.int32, device=dev)
+            self.rij = torch.empty(self.P, 3, dtype=torch.float64, device=dev)
+            self.rowptr = torch.empty(self.nl + 1, dtype=torch.int32, device=dev)
+            self.bounds = bounds.numpy()
         else:
+            pi = torch.as_tensor(pair_i, device=dev).to(torch.int32)
             pj = torch.as_tensor(pair_j, device=dev).to(torch.int32)
-            rij = torch.as_tensor(rij, device=dev).to(torch.float64)
+            rr = torch.as_tensor(rij, device=dev).to(torch.float64)
+            ordered = self.P <= 1 or bool((pi[1:] >= pi[:-1]).all())
             if not ordered:
                 o = torch.argsort(pi, stable=True)
-                pi, pj, rij = pi[o], pj[o], rij[o]
+                pi, pj, rr = pi[o], pj[o], rr[o]
                 self.perm = o.to(torch.int64).contiguous()
-        self.pi, self.pj, self.rij = pi.contiguous(), pj.contiguous(), rij.reshape(-1, 3).contiguous()
-        self.nl, self.nt = int(nl), int(nt)
-        self.rowptr = torch.searchsorted(pi, torch.arange(nl + 1, device=dev, dtype=torch.int32)).to(torch.int32)
+            self.pi, self.pj, self.rij = pi.contiguous(), pj.contiguous(), rr.reshape(-1, 3).contiguous()
+            self.rowptr = torch.searchsorted(pi, torch.arange(self.nl + 1, device=dev, dtype=torch.int32)).to(torch.int32)
+            e_off = self.rowptr[bounds.to(dev)].to(torch.int64).cpu().numpy()
+            if self.P and (e_off[0] != 0 or e_off[-1] != self.P):
+                raise RuntimeError(f"Plan: pair_i holds receivers outside [0, nlocal = {self.nl})")
+        self.e_off = e_off                                              # edge range of every chunk (host)
         el = torch.as_tensor(elems, device=dev).to(torch.int64)
-        spec = eng.col2s[el]
-        if bool((spec < 0).any()):
-            raise RuntimeError("Plan: an atom's species has no tables in this engine (rebuild it with that species)")
+        zn = eng.col2s.numel()
+        spec = torch.where((el >= 0) & (el < zn), eng.col2s[el.clamp(0, zn - 1)], -1)
         self.spec = spec.to(torch.int32).contiguous()
-        C_ = eng.chunk
         S = eng.fm.S
-        nch = (nl + C_ - 1) // C_
-        cid = torch.arange(nl, device=dev) // C_
-        key = cid * S + self.spec[:nl].long()
+        cid = torch.arange(self.nl, device=dev) // C_
+        key = cid * S + self.spec[:self.nl].long()
         og = torch.argsort(key, stable=True)
         self.order = (og - cid[og] * C_).to(torch.int32).contiguous()
-        cnt = torch.bincount(key, minlength=max(nch * S, 1)).view(max(nch, 1), S).cpu().numpy()
+        # one device -> host read: species counts per chunk plus the number of atoms without tables
+        cnt = torch.cat([torch.bincount(key, minlength=max(nch * S, 1)), (spec < 0).sum().view(1)]).cpu().numpy()
+        if cnt[-1]:
+            raise RuntimeError("Plan: an atom's species has no tables in this engine (rebuild it with that species)")
+        cnt = cnt[:-1].reshape(max(nch, 1), S)
         off = np.zeros((max(nch, 1), S + 1), dtype=np.int32)
         off[:, 1:] = np.cumsum(cnt, 1)
         self.spec_off = np.ascontiguousarray(off.reshape(-1))
-        self.n_chunks = nch
-        bounds = torch.clamp(torch.arange(nch + 1, device=dev) * C_, max=nl)
-        self.e_off = self.rowptr[bounds].to(torch.int64).cpu().numpy()   # edge range of every chunk (host)
+
+    def sorted_copy(self, eng: "ThreePassEngine") -> "Plan":
+        """The same inputs copied to the device and sorted there (after MB_ST_UNSORTED from a streamed plan)."""
+        return Plan(eng, *self._inputs, self.nl, self.nt, stream_host=False)
+
+
+def _pinned(t, dtype) -> bool:
+    return isinstance(t, torch.Tensor) and not t.is_cuda and t.is_pinned() and t.dtype == dtype and t.is_contiguous()
 
 
 class ThreePassEngine:
@@ -357,6 +383,10 @@ class ThreePassEngine:
         self._buf = {}
         self._cap = {}
         self._io = None                   # side stream of the host <-> device copies
+        self.pass_timing = False          # record CUDA events between the passes (pass_times())
+        self._marks = None
+        self._marks_valid = False
+        self._h2d_marks = None
         self._ev_cache = {}
         self.host_pf_written = False
 
@@ -407,33 +437,67 @@ class ThreePassEngine:
             names = [n for bit, n in ((1, "sender index out of range"), (2, "species out of range"),
                                       (4, "bad CSR row pointer"), (8, "non-finite or zero edge vector"),
                                       (16, "pair_i does not match its CSR row"),
-                                      (32, "tensor-core GEMM barrier wait expired")) if s & bit]
+                                      (32, "tensor-core GEMM barrier wait expired"),
+                                      (64, "pair_i not sorted by receiver")) if s & bit]
             raise RuntimeError(f"mace_b200 {what}: input error reported by the kernels: {', '.join(names)}")
 
     # ------------------------------------------------------------------------------------------------ evaluation
-    def _run(self, plan, ev, b, forward_exchange=None, reverse_exchange=None):
+    def _run(self, plan, ev, b, forward_exchange=None, reverse_exchange=None, zero_status=True):
         """The device work of one evaluation on the current stream (capturable when there is no exchange)."""
         L = N.lib()
         m = N.byref(self.fm.struct)
         evp = N.byref(ev)
         st = torch.cuda.current_stream(self.device).cuda_stream
-        b["status"].zero_()
+        if zero_status:
+            b["status"].zero_()
         b["eat"].zero_()
         PFd = self._get("PFd", (plan.P, 3), torch.float64)
         fbits = self._get("fmax", (1,), torch.int32)
         fbits.zero_()
         if ev.done_ev:                                   # pass C hands out every finished chunk's pair forces
             ev.pf_out, ev.fmax_bits = N.ptr(PFd), N.ptr(fbits)
+        marks = self._pass_marks() if self.pass_timing and not torch.cuda.is_current_stream_capturing() else None
+        self._marks_valid = marks is not None
+        mark = (lambda k: marks[k].record()) if marks else (lambda k: None)
+        mark(0)
         N.check(L.mace_b200_pass_a(m, evp, st), "pass_a")
+        mark(1)
         if forward_exchange is not None and plan.nt > plan.nl:
             forward_exchange(b["H1"].view(plan.nt, 4 * C))
+        mark(2)
         N.check(L.mace_b200_x2_all(m, evp, st), "x2_all")
         N.check(L.mace_b200_pass_b(m, evp, st), "pass_b")
+        mark(3)
         if reverse_exchange is not None and plan.nt > plan.nl:
             reverse_exchange(b["G1"].view(plan.nt, 4 * C))
+        mark(4)
         N.check(L.mace_b200_pass_c(m, evp, st), "pass_c")
+        mark(5)
         N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
+        mark(6)
         return PFd, fbits
+
+    _PASSES = ("A", "xchg_fwd", "B", "xchg_rev", "C", "finalize")
+
+    def _pass_marks(self):
+        if self._marks is None:
+            self._marks = [torch.cuda.Event(enable_timing=True) for _ in range(len(self._PASSES) + 1)]
+        return self._marks
+
+    def pass_times(self) -> dict:
+        """Seconds of each pass of the last eager evaluation (CUDA events; needs pass_timing = True before it ran,
+        the per-pass timers of the reference's log, mliap_threepass.py:488-587).  Synchronises."""
+        if not self._marks or not self._marks_valid:
+            return {}
+        self._marks[-1].synchronize()
+        out = {f"t_{name}": self._marks[k].elapsed_time(self._marks[k + 1]) * 1e-3
+               for k, name in enumerate(self._PASSES)}
+        if self._h2d_marks is not None:           # streamed pair list: its side-stream copies (all chunks)
+            self._h2d_marks[1].synchronize()
+            out["t_h2d_pairs"] = self._h2d_marks[0].elapsed_time(self._h2d_marks[1]) * 1e-3
+            out["t_h2d_pairs_after_A_start"] = self._marks[0].elapsed_time(self._h2d_marks[1]) * 1e-3
+            self._h2d_marks = None
+        return out
 
     def _events(self, key, n):
         evs = self._ev_cache.get(key)
@@ -467,22 +531,33 @@ class ThreePassEngine:
             cur = torch.cuda.current_stream(self.device)
             e_off, nch = plan.e_off, plan.n_chunks
             keep = []
+            b["status"].zero_()                           # before the side stream's CSR checks can set bits
             if deferred or host_pf is not None:
                 if self._io is None:
                     self._io = torch.cuda.Stream(self.device)
                 io = self._io
                 io.wait_stream(cur)
             if deferred:
-                h_pj, h_rij = plan.host_src
+                L = N.lib()
+                h_pi, h_pj, h_rij = plan.host_src
                 waits = self._events("wait", nch)
                 with torch.cuda.stream(io):
+                    if self.pass_timing:
+                        self._h2d_marks = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                        self._h2d_marks[0].record(io)
                     for k in range(nch):
                         e0, e1 = int(e_off[k]), int(e_off[k + 1])
+                        plan.pi[e0:e1].copy_(h_pi[e0:e1], non_blocking=True)
                         plan.pj[e0:e1].copy_(h_pj[e0:e1], non_blocking=True)
                         plan.rij[e0:e1].copy_(h_rij[e0:e1], non_blocking=True)
+                        N.check(L.mace_b200_csr_rows(N.ptr(plan.pi), e0, e1, int(plan.bounds[k]),
+                                                     int(plan.bounds[k + 1]), N.ptr(plan.rowptr), N.ptr(b["status"]),
+                                                     io.cuda_stream), "csr_rows")
                         waits[k].record(io)
-                plan.pj.record_stream(io)
-                plan.rij.record_stream(io)
+                    if self.pass_timing:
+                        self._h2d_marks[1].record(io)
+                for t in (plan.pi, plan.pj, plan.rij, plan.rowptr, b["status"]):
+                    t.record_stream(io)
                 arr = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in waits])
                 keep.append(arr)
                 ev.wait_ev = N.ctypes.addressof(arr)
@@ -492,7 +567,7 @@ class ThreePassEngine:
                 arr2 = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in done])
                 keep.append(arr2)
                 ev.done_ev = N.ctypes.addressof(arr2)
-            PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange)
+            PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange, zero_status=False)
             if out_host:
                 with torch.cuda.stream(io):
                     for k in range(nch):
@@ -504,6 +579,9 @@ class ThreePassEngine:
             if deferred or out_host:
                 cur.wait_stream(io)
         self._last = b
+        if deferred and int(b["status"].item()) & N.ST_UNSORTED:
+            # the streamed pair list was not receiver-sorted after all: evaluate again from a sorted device copy
+            return self.evaluate(plan.sorted_copy(self), forward_exchange, reverse_exchange, check, graph, host_pf)
         if check:
             self._check_status(b, "evaluation")
         self.fmax = float(fbits.view(torch.float32).item()) if check else None
@@ -545,6 +623,7 @@ class ThreePassEngine:
             if plan.perm is not None:
                 st.perm.copy_(plan.perm, non_blocking=True)
         g["graph"].replay()
+        self._marks_valid = False
         return g["b"], g["PFd"], g["fbits"]
 
     def owner_exchange(self, owner, nl: int):

@@ -83,7 +83,7 @@ class ThreePassMLIAP(MLIAPUnified):
         self._dev = dev
         if os.environ.get("MACE3P_CHUNK"):
             self.chunk = int(os.environ["MACE3P_CHUNK"])
-        cols = sorted(int(c) for c in torch.unique(elems).tolist())
+        cols = sorted(int(c) for c in torch.unique(elems.long()).tolist())
         self._cols = cols
         self._eng = ThreePassEngine(self.model, cols, chunk=self.chunk, spline_grid=self.spline_grid or 512,
                                     device=dev)
@@ -94,6 +94,7 @@ class ThreePassMLIAP(MLIAPUnified):
         self._fmax_abort = float(os.environ.get("MACE3P_FMAX_ABORT", "100.0"))
         path = os.environ.get("MACE3P_LOG")
         self._log = open(path, "a", buffering=1) if path else None
+        self._eng.pass_timing = self._log is not None
 
     # ------------------------------------------------------------------------------------------------ entry point
     def compute_forces(self, data):
@@ -110,19 +111,21 @@ class ThreePassMLIAP(MLIAPUnified):
             raise RuntimeError(f"ThreePassMLIAP guard: nlocal={nl:,}, pairs={P:,} -> estimated LAMMPS neighbour slots "
                                f"{est_slots:.3e} is close to the 2^31 int32 limit of the Kokkos neighbour list "
                                f"(skin {skin} A). Use fewer atoms per GPU, a smaller skin, or more GPUs.")
-        elems = torch.as_tensor(data.elems).long()
-        if not hasattr(self, "_eng") or not set(torch.unique(elems).tolist()) <= set(self._cols):
+        elems = torch.as_tensor(data.elems)
+        if not hasattr(self, "_eng"):
             self._setup(elems)
         self.step += 1
+        # pinned host pair arrays stay on the host: the engine streams them in chunk by chunk during pass A
+        pi, pj, rij = (torch.as_tensor(x) for x in (data.pair_i, data.pair_j, data.rij))
+        try:
+            plan = self._eng.plan(pi, pj, rij, elems.to(self._dev, non_blocking=True), nl, nt)
+        except RuntimeError as err:
+            if "has no tables" not in str(err):
+                raise
+            self._setup(elems)                      # a species appeared that the tables were not built for
+            plan = self._eng.plan(pi, pj, rij, elems.to(self._dev, non_blocking=True), nl, nt)
         eng = self._eng
-        dev = self._dev
-        pi = torch.as_tensor(data.pair_i).to(dev, non_blocking=True)
-        pj = torch.as_tensor(data.pair_j)
-        rij = torch.as_tensor(data.rij)
-        if pj.is_cuda or rij.is_cuda or not (pj.is_pinned() and rij.is_pinned()):
-            pj, rij = pj.to(dev, non_blocking=True), rij.to(dev, non_blocking=True)
-        # pinned host senders / vectors stay on the host: the engine streams them in chunk by chunk during pass A
-        plan = eng.plan(pi, pj, rij, elems.to(dev, non_blocking=True), nl, nt)
+        t_prep = time.perf_counter() - t_start
         hbuf = getattr(data, "pair_forces_host", None)
         D = 512
 
@@ -148,10 +151,14 @@ class ThreePassMLIAP(MLIAPUnified):
         data.update_pair_forces_gpu(hbuf if eng.host_pf_written else PF)
         if self._log is not None:
             torch.cuda.synchronize()
+            peak = torch.cuda.max_memory_allocated(self._dev) / 1e9
+            torch.cuda.reset_peak_memory_stats(self._dev)
             self._log.write(json.dumps(dict(step=self.step, nlocal=nl, ntotal=nt, npairs=P,
                                             chunks=(nl + self.chunk - 1) // self.chunk,
-                                            sorted_pairs=plan.perm is None, t_total=time.perf_counter() - t_start,
-                                            t_gap_lammps=t_gap, fmax=fmax)) + "\n")
+                                            sorted_pairs=plan.perm is None, streamed_pairs=plan.host_src is not None,
+                                            graphs=bool(eng.graphs), captures=eng.captures,
+                                            t_total=time.perf_counter() - t_start, t_prep=t_prep, **eng.pass_times(),
+                                            t_gap_lammps=t_gap, peak_gb=peak, fmax=fmax)) + "\n")
         self._t_end = time.perf_counter()
 
     def compute_descriptors(self, data):
