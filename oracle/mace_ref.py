@@ -16,7 +16,8 @@ What it restates (reference citations are paths inside ShiQiaoL/mace-million):
   loss = E1 + G1 . h1), on the ML-IAP data model (receivers local, senders local or ghost, pair forces dE/drij);
 * the tabulated radial weights of ``mace_onegpu/conv_spline.py:230-249`` / ``mace_onegpu/spline_radial.py:237-272``
   (fp64 samples on M knots over [0.5, r_max], dW/dr by central differences with eps = 1e-5 (r_hi - r_lo), cubic Hermite
-  evaluation with x clamped to [0, M - 1 - 1e-4] as in ``mace_onegpu/spline_w.py:18-27``).
+  evaluation with x clamped to [0, M - 1 - 1e-4] as in ``mace_onegpu/spline_w.py:18-27``, the derivative taken at
+  the clamped point as the reference's backward kernel does, ``spline_w.py:53-75``).
 
 Parity with mace-torch / e3nn itself is unpinned (neither library is installed); the invariants the reference's own
 tests check (three-pass == full graph, chunk invariance, periodic replica, fp32 vs fp64) plus rotation / inversion
@@ -134,7 +135,11 @@ class MaceRef:
         if self.tables is None:
             return self.radial_mlp(i, feats)
         t = self.tables[i]
-        x = ((r.reshape(-1) - self.r_lo) / t["h"]).clamp(0.0, t["M"] - 1 - 1e-4)
+        # x clamped to [0, M - 1 - 1e-4] (spline_w.py:19-27); the derivative is the interpolant's slope at the clamped
+        # point times 1/h, also where x was clamped (r < r_lo): the reference's backward evaluates dW/dt at the clamped
+        # t and scales it by inv_h unconditionally (spline_w.py:53-75, _w_bwd), so the clamp passes gradients through
+        x = (r.reshape(-1) - self.r_lo) / t["h"]
+        x = x.detach().clamp(0.0, t["M"] - 1 - 1e-4) + (x - x.detach())
         k = x.detach().floor().long()
         s = (x - k.to(x.dtype)).unsqueeze(-1)
         s2, s3 = s * s, s * s * s
