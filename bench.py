@@ -58,6 +58,7 @@ FLOPS_PER_EDGE_L1D = {"edge_l1_fwd": 8 * 64 + 2 * 64 * 16, "edge_l1_bwd": 8 * 64
 # --steps 1 --warmup 1 --no-e2e --no-cpu-baseline`): a 16,384-receiver chunk of the 1.03M-atom water box.
 TRAFFIC_PER_LAUNCH = {("water_1m", 16384, "edge_l2_bwd"): 703.40e6 + 149.40e6}
 EDGE_PASSES = {"edge_l1_fwd": 1, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
+ORDER = "morton"      # atom order of the synthetic boxes (--order)
 
 
 def parse():
@@ -70,23 +71,35 @@ def parse():
     ap.add_argument("--chunk", type=int, default=16384)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-replica-check", action="store_true", help="multi-GPU: skip the single-GPU comparison")
     ap.add_argument("--cpu-sample", type=int, default=6, help="water molecules per box edge of the CPU sample")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--skin", type=float, default=2.0, help="ghost shell = r_max + skin (multi-GPU)")
+    ap.add_argument("--order", default="morton", choices=["morton", "grid"],
+                    help="atom order: Morton curve of 3 A cells (spatially sorted, as MD engines pass atoms) or the "
+                         "generator's grid order")
     args = ap.parse_args()
+    global ORDER
+    ORDER = args.order
     if args.warmup < 1 or args.steps < 1:
         ap.error("--warmup and --steps must be >= 1 (the per-kernel breakdown is taken from the last warm-up step)")
     return args
 
 
 def build_structure(cfg, grid=(1, 1, 1)):
+    """The configuration's box; with grid != (1, 1, 1) its exact periodic replica (weak scaling): every rank's domain
+    is then a copy of the single-GPU box, so each rank knows its atoms' energies and forces from one single-GPU
+    evaluation (the reference's periodic-replica check, tests/gpu/test_threepass.py:80-87)."""
     from mace_onegpu import structures as S
 
     if cfg["kind"] == "water":
-        return S.water_box(cfg["n"] * grid[0], cfg["n"] * grid[1], cfg["n"] * grid[2], seed=cfg["seed"])
-    if tuple(grid) != (1, 1, 1):
-        raise ValueError("weak scaling is defined for the water boxes")
-    return S.alloy_bcc(cfg["n"], seed=cfg["seed"])
+        cell = S.water_box(cfg["n"], seed=cfg["seed"])
+    else:
+        cell = S.alloy_bcc(cfg["n"], seed=cfg["seed"])
+    if ORDER == "morton":
+        o = S.morton_order(cell[0], cell[2])
+        cell = (cell[0][o], cell[1][o], cell[2])
+    return cell if tuple(grid) == (1, 1, 1) else S.tile(*cell, grid)
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -188,6 +201,51 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ replica check
+def replica_check(args, cfg, m, dev, eng, step, hx, gid, n, nt, pi, pj, n_cell):
+    """Multi-GPU correctness inside every scaling run.  Each rank evaluates the single-GPU box (the weak-scaling
+    cell, or the whole box under strong scaling) on its own GPU, then compares its domain's last distributed
+    evaluation atom by atom: energy of every local atom against its image's, atom force (ghost contributions
+    returned to their owners by a reverse halo exchange) against its image's, and the total energy against N times
+    (weak) or once (strong) the single-GPU total.  Collective steps are the same on every rank."""
+    import torch
+    import torch.distributed as dist
+
+    from mace_onegpu import neighbors as NB
+    from mace_onegpu import structures as S
+    from mace_onegpu.engine import ThreePassEngine
+
+    eat, pf = step()
+    eat = eat.clone()
+    F = torch.zeros(nt, 3, dtype=torch.float32, device=dev)
+    F.index_add_(0, pi.long(), (-pf).float())
+    F.index_add_(0, pj.long(), pf.float())
+    hx.reverse(F)
+    cpos, cZ, cbox = build_structure(cfg)
+    ccols = torch.as_tensor(S.species_columns(cZ, m.arch.atomic_numbers))
+    rpi, rpj, rrij = NB.neighbor_list(cpos, cbox, m.arch.r_max, device=dev)
+    reng = ThreePassEngine(m, sorted(set(ccols.tolist())), chunk=args.chunk, device=dev)
+    reat, rpf = reng.evaluate(reng.plan(rpi, rpj, rrij, ccols.to(dev), n_cell, n_cell))
+    rF = torch.zeros(n_cell, 3, dtype=torch.float64, device=dev)
+    rF.index_add_(0, rpi.long(), -rpf)
+    rF.index_add_(0, rpj.long(), rpf)
+    img = torch.as_tensor(gid[:n] % n_cell, device=dev)
+    stats = torch.tensor([(eat - reat[img]).abs().max().item(), (F[:n].double() - rF[img]).abs().max().item()],
+                         dtype=torch.float64, device=dev)
+    esum = torch.tensor([eat.sum().item()], dtype=torch.float64, device=dev)
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    dist.all_reduce(esum)
+    copies = dist.get_world_size() if args.scaling == "weak" else 1
+    e1 = float(reat.sum().item())
+    del reng
+    torch.cuda.empty_cache()
+    return {"max_dE_eV": stats[0].item(), "max_dF_eV_per_A": stats[1].item(), "E_total_eV": esum.item(),
+            "E_single_gpu_x_copies_eV": copies * e1, "rel_dE_total": abs(esum.item() - copies * e1) / abs(copies * e1),
+            "tolerance": {"dE_eV": 1e-5, "dF_eV_per_A": 1e-3},
+            "ok": bool(stats[0].item() < 1e-5 and stats[1].item() < 1e-3),
+            "reference": f"single-GPU evaluation of the {n_cell}-atom periodic box on every rank"}
+
+
 # ------------------------------------------------------------------------------------------------ B200 arm
 def main():
     args = parse()
@@ -238,6 +296,7 @@ def main():
 
         grid = DM.grid_for(world)
         pos, Z, box = build_structure(cfg, grid if args.scaling == "weak" else (1, 1, 1))
+        n_cell = len(Z) // (world if args.scaling == "weak" else 1)
         cols_all = torch.as_tensor(S.species_columns(Z, m.arch.atomic_numbers))
         dec = DM.Decomposition(pos, box, grid, m.arch.r_max + args.skin)
         p, gid, n = dec.rank_atoms(rank)
@@ -335,6 +394,15 @@ def main():
             ems = float(tt.item())
         e2e = {"value": n_total * args.steps / (ems * 1e-3), "unit": "atoms/s",
                "h2d_bytes_per_step": int(P * (4 + 4 + 24) + nt * 8), "d2h_bytes_per_step": int(n * 8 + P * 24)}
+        # one more call with CUDA events between the passes and around the streamed pair-list copies (not timed)
+        mli._eng.pass_timing = True
+        mli.compute_forces(data)
+        e2e["breakdown_s"] = {k: round(v, 5) for k, v in mli._eng.pass_times().items()}
+        mli._eng.pass_timing = False
+
+    replica = None
+    if world > 1 and not args.no_replica_check:
+        replica = replica_check(args, cfg, m, dev, eng, step, hx, gid, n, nt, pi, pj, n_cell)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -358,14 +426,15 @@ def main():
                            "parallelism": parallelism, "gemm": "tcgen05 3xTF32" if eng.fm.use_tc else "SIMT fp32",
                            "layer1": "density projection" if eng.fm.l1_density else "direct",
                            "host_numa_bound": numa,
-                           "l2": "inputs larger than L2 (no flush)"},
+                           "l2": "inputs larger than L2 (no flush)", "atom_order": ORDER},
                 "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak,
                              "traffic": TRAFFIC_PER_LAUNCH.get((args.config, args.chunk, dom)),
                              "traffic_unit": "bytes per launch (ncu dram__bytes_read + dram__bytes_write)",
                              "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",
                              "flops_per_edge": fpe[dom]},
-                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds}
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds,
+                "replica_check": replica}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -57,6 +57,39 @@ def alloy_bcc(n: int = 60, a: float = 3.0, seed: int = 0, disp: float = 0.1, zs=
     return np.remainder(pos, box), Z, box
 
 
+def tile(pos, Z, box, reps):
+    """Periodic replica of a box: reps = (rx, ry, rz) copies along each axis.  Atom k of copy c = (cx, cy, cz) (copies
+    in C order, z fastest) gets index c * n + k and position pos[k] + c * box, so every replica atom's environment is
+    its image's environment in the original periodic box."""
+    pos = np.asarray(pos, dtype=np.float64)
+    box = np.asarray(box, dtype=np.float64)
+    shifts = np.stack(np.meshgrid(*[np.arange(r) for r in reps], indexing="ij"), -1).reshape(-1, 3) * box
+    P = (shifts[:, None, :] + pos[None, :, :]).reshape(-1, 3)
+    return P, np.tile(np.asarray(Z), len(shifts)), box * np.asarray(reps, dtype=np.float64)
+
+
+def _spread3(v: np.ndarray) -> np.ndarray:
+    """Bits of v (< 2^21) moved to every third position (bit b -> bit 3 b)."""
+    v = v.astype(np.uint64) & np.uint64(0x1FFFFF)
+    for shift, mask in ((32, 0x1F00000000FFFF), (16, 0x1F0000FF0000FF), (8, 0x100F00F00F00F00F),
+                        (4, 0x10C30C30C30C30C3), (2, 0x1249249249249249)):
+        v = (v | (v << np.uint64(shift))) & np.uint64(mask)
+    return v
+
+
+def morton_order(pos, box, cell: float = 3.0) -> np.ndarray:
+    """Permutation that sorts atoms along a Z-order (Morton) curve of cubic cells of about `cell` A, atoms of one cell
+    keeping their relative order.  Spatially sorted atoms are what a production MD engine passes (LAMMPS re-sorts
+    atoms spatially every 1000 steps by default; the reference's standalone driver orders them on a Morton curve
+    too, mace_onegpu/receiver_chunk_mace.py:100-104): receivers that are close in index then share senders, so
+    the senders' feature rows are reused from L2."""
+    pos = np.remainder(np.asarray(pos, dtype=np.float64), box)
+    nc = np.maximum(np.floor(np.asarray(box) / cell).astype(np.int64), 1)
+    c = np.minimum((pos / (np.asarray(box) / nc)).astype(np.int64), nc - 1)
+    code = (_spread3(c[:, 0]) << np.uint64(2)) | (_spread3(c[:, 1]) << np.uint64(1)) | _spread3(c[:, 2])
+    return np.argsort(code, kind="stable")
+
+
 def species_columns(Z, atomic_numbers) -> np.ndarray:
     """Model one-hot column of every atom (index into atomic_numbers)."""
     lut = {int(z): i for i, z in enumerate(atomic_numbers)}

@@ -9,10 +9,10 @@ as in the reference's fp32-vs-fp64 check (tests/gpu/test_threepass.py:90-94).
   GEMM paths (tcgen05 3xTF32 and SIMT fp32);
 * dense: more than 256 neighbours per receiver, so the layer-2 edge kernels loop over three 128-edge batches, and
   pairs as close as 0.18 A, below the spline's first knot (0.5 A), where the clamped interpolant's slope is used as
-  in the reference's backward kernel (spline_w.py:53-75).  At 3.7x water's density its per-atom energies carry
-  3.7x larger messages: the SIMT GEMM path meets the absolute 1e-5 eV, the tcgen05 3xTF32 path (about 2^-21
-  relative error per product) is held to 1e-5 relative to the atom's energy (measured 2.1e-5 eV on atoms of up to
-  3.3 eV).
+  in the reference's backward kernel (spline_w.py:53-75).  At 3.7x water's density the messages summed per receiver
+  are 3.7x larger: the SIMT GEMM path meets the absolute 1e-5 eV (measured 4.4e-6 eV), while the tcgen05 3xTF32
+  path (about 2^-21 relative error per product against fp32's 2^-24) is held to 3e-5 eV here (measured 2.1e-5 eV);
+  both stay within 1e-3 eV/A on the forces.
 The structures are regenerated from their seeds and checked against the fixture's position checksum first."""
 import os
 
@@ -31,6 +31,7 @@ from oracle import mace_ref
 pytestmark = pytest.mark.gpu
 
 E_TOL = 1e-5      # eV per atom
+E_TOL_DENSE_TC = 3e-5   # eV per atom: the 3.7x-density stress case on the tcgen05 3xTF32 GEMM path (see above)
 F_TOL = 1e-3      # eV / A
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
@@ -57,7 +58,7 @@ def load(name):
                 F=torch.as_tensor(g["F"]).double(), max_nbr=int(g["max_neighbors"]))
 
 
-def _compare(s, eat, pf, pi=None, pj=None, e_rel=False):
+def _compare(s, eat, pf, pi=None, pj=None, dense_tc=False):
     pi = s["pi"] if pi is None else pi
     pj = s["pj"] if pj is None else pj
     F = mace_ref.atom_forces(pi.cpu(), pj.cpu(), torch.as_tensor(pf).double().cpu(), s["n"])
@@ -65,10 +66,7 @@ def _compare(s, eat, pf, pi=None, pj=None, e_rel=False):
     de = err.max().item()
     dF = (F - s["F"]).abs().max().item()
     print(f"max|dE_i| {de:.3e} eV  max|dF| {dF:.3e} eV/A  (|F|max {s['F'].abs().max().item():.2f})")
-    if e_rel:
-        assert bool((err < E_TOL * torch.clamp(s["eat"].abs(), min=1.0)).all())
-    else:
-        assert de < E_TOL
+    assert de < (E_TOL_DENSE_TC if dense_tc else E_TOL)
     assert dF < F_TOL
 
 
@@ -121,4 +119,4 @@ def test_dense_multi_batch(use_tc):
     nbr = torch.bincount(s["pi"].long(), minlength=s["n"])
     assert int(nbr.max()) == s["max_nbr"] and int(nbr.min()) > 256              # >= 3 batches of 128 edges
     _, eat, pf = _evaluate(s, 512, use_tc=use_tc)
-    _compare(s, eat, pf, e_rel=use_tc)
+    _compare(s, eat, pf, dense_tc=use_tc)
