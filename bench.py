@@ -53,10 +53,12 @@ FLOPS_PER_EDGE = {"edge_l1_fwd": 8 * 512 + 2 * 128 * 16 + 128 * 4,
 FLOPS_PER_EDGE_L1D = {"edge_l1_fwd": 8 * 64 + 2 * 64 * 16, "edge_l1_bwd": 8 * 64 + 4 * 64 * 16}
 # edge-kernel launches per evaluation: pass A l1_fwd, pass B l2_fwd + l2_bwd, pass C l1_bwd (pass C reads pass A's
 # layer-1 results from the x1 cache, which the engine keeps whenever it fits)
-# DRAM traffic of one launch of the dominant kernel, from a one-pass ncu capture of this bench's own command
-# (`ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:k_edge_l2_bwd -s 10 -c 1 python bench.py
-# --steps 1 --warmup 1 --no-e2e --no-cpu-baseline`): a 16,384-receiver chunk of the 1.03M-atom water box.
-TRAFFIC_PER_LAUNCH = {("water_1m", 16384, "edge_l2_bwd"): 703.40e6 + 149.40e6}
+# DRAM traffic of one launch of the dominant kernel: dram__bytes_read.sum + dram__bytes_write.sum of one
+# 16,384-receiver k_edge_l2_bwd launch of the 24k-atom box (`ncu --set full --clock-control none -k regex:k_edge_l2_bwd
+# -c 1 python bench.py --config water_24k --steps 1 --warmup 1 --no-e2e --no-cpu-baseline`), scaled per receiver to
+# the 1.03M-atom box's 16,384-receiver chunks (same 84.6 edges per receiver).
+TRAFFIC_PER_LAUNCH = {("water_24k", 16384, "edge_l2_bwd"): 560.42e6 + 82.16e6,
+                      ("water_1m", 16384, "edge_l2_bwd"): 560.42e6 + 82.16e6}
 EDGE_PASSES = {"edge_l1_fwd": 1, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
 ORDER = "morton"      # atom order of the synthetic boxes (--order)
 
