@@ -433,6 +433,8 @@ def main():
                              "frac": achieved / peak,
                              "traffic": TRAFFIC_PER_LAUNCH.get((args.config, args.chunk, dom)),
                              "traffic_unit": "bytes per launch (ncu dram__bytes_read + dram__bytes_write)",
+                             "traffic_source": "one-launch capture on the 24k-atom box (16,384 receivers), scaled per "
+                                               "receiver (profiles/k_edge_l2_bwd_water24k.md)",
                              "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",
                              "flops_per_edge": fpe[dom]},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds,
