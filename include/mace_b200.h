@@ -212,19 +212,23 @@ int mace_b200_edge_l1_bwd(const mb_model_t* m, const mb_eval_t* ev, int32_t a, i
 
 /* ---------------------------------------------------------------- generic fused convolution (FusedConvTP)
  * Replaces the cuEquivariance fused convolution behind FusedConvTP.forward (mace_onegpu/fused_conv.py:20-37) and its
- * autograd backward: out[receiver[e]][o][:] += sum_terms coef W[e][w][:] X[sender[e]][k][:] Y[e][m] with explicit
- * per-edge weights W [E][nW][128], node features X [n][nX][128], edge attributes Y [E][nY]; terms_wkmo [n_terms][4]
- * = (w, k, m, o) with coef [n_terms].  out must be zeroed by the caller (accumulated atomically; any edge order).
- * bwd: given g = dL/dout [n][nO][128] accumulates dX (atomic), dY (atomic) and dW (dW[e] owned per edge); any of the
- * three may be null.  Out-of-range node indices set MB_ST_BAD_SENDER in *status (may be null) and skip the edge. */
+ * autograd backward: out[receiver[e]][o][:] = sum over the receiver's edges and the terms of coef W[e][w][:]
+ * X[sender[e]][k][:] Y[e][m], with explicit per-edge weights W [E][nW][128], node features X [n][nX][128] and edge
+ * attributes Y [E][nY]; terms_wkmo [n_terms][4] = (w, k, m, o) with coef [n_terms] (any channelwise path table).
+ * Edges are visited through CSR lists the caller builds: recv_rowptr [n + 1] / recv_edges (edge ids grouped by
+ * receiver), and for dX send_rowptr / send_edges (grouped by sender), so no kernel uses atomics and the results are
+ * deterministic.  fwd writes every output row (no zeroing needed).  bwd: given g = dL/dout [n][nO][128] writes
+ * dW [E][nW][128], dY [E][nY] and dX [n][nX][128]; any of the three may be null.  Out-of-range node indices set
+ * MB_ST_BAD_SENDER / MB_ST_BAD_RECEIVER in *status (may be null) and skip the edge. */
 int mace_b200_conv_tp_fwd(const float* X, int32_t nX, const float* Y, int32_t nY, const float* W, int32_t nW,
-                          const int32_t* sender, const int32_t* receiver, int64_t E, int32_t n_nodes,
-                          const int32_t* terms_wkmo, const float* coef, int32_t n_terms, float* out, int32_t nO,
-                          uint32_t* status, void* stream);
+                          const int32_t* sender, const int64_t* recv_rowptr, const int64_t* recv_edges,
+                          int32_t n_nodes, const int32_t* terms_wkmo, const float* coef, int32_t n_terms, float* out,
+                          int32_t nO, uint32_t* status, void* stream);
 int mace_b200_conv_tp_bwd(const float* X, int32_t nX, const float* Y, int32_t nY, const float* W, int32_t nW,
-                          const int32_t* sender, const int32_t* receiver, int64_t E, int32_t n_nodes,
-                          const int32_t* terms_wkmo, const float* coef, int32_t n_terms, const float* g, int32_t nO,
-                          float* dX, float* dY, float* dW, uint32_t* status, void* stream);
+                          const int32_t* sender, const int32_t* receiver, const int64_t* recv_rowptr,
+                          const int64_t* recv_edges, const int64_t* send_rowptr, const int64_t* send_edges,
+                          int32_t n_nodes, const int32_t* terms_wkmo, const float* coef, int32_t n_terms,
+                          const float* g, int32_t nO, float* dX, float* dY, float* dW, uint32_t* status, void* stream);
 
 /* ---------------------------------------------------------------- node GEMM
  * Replaces the cuEquivariance irreps Linear and SpeciesSkip.forward (mace_onegpu/fast_layers.py:96-105):

@@ -61,10 +61,10 @@ _SIGS = {
     "mace_b200_edge_l2_fwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
     "mace_b200_edge_l2_bwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
     "mace_b200_edge_l1_bwd": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
-    "mace_b200_conv_tp_fwd": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_vp, c_vp,
+    "mace_b200_conv_tp_fwd": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp,
                                       c_i32, c_vp, c_i32, c_vp, c_vp]),
-    "mace_b200_conv_tp_bwd": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_vp, c_vp,
-                                      c_i32, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mace_b200_conv_tp_bwd": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                      c_i32, c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mace_b200_node_gemm": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp,
                                     c_i32, c_vp]),
     "mace_b200_node_gemm_tc": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32,
@@ -112,6 +112,60 @@ def lib():
                                f"{ctypes.sizeof(MBModel)}/{ctypes.sizeof(MBEval)}")
         _lib = L
     return _lib
+
+
+OPS_PATH = os.path.join(_HERE, "_lib", "libmace_b200_torch.so")
+OPS = ("conv_tp", "conv_tp_backward", "build_tables", "edge_l1_fwd", "edge_l1_bwd", "edge_l2_fwd", "edge_l2_bwd",
+       "node_gemm", "symcon_fwd", "symcon_bwd", "pack_halo", "unpack_halo_add", "csr_rows", "guard")
+_ops = None
+
+
+def ops():
+    """torch.ops.mace_b200: the TORCH_LIBRARY custom ops of libmace_b200_torch.so over this library's C ABI (loaded
+    once; raises if it was not built: there is no fallback)."""
+    global _ops
+    if _ops is None:
+        import torch
+
+        lib()
+        if not os.path.exists(OPS_PATH):
+            raise RuntimeError(f"{OPS_PATH} is missing: build it with `python mace-million_b200/build.py`")
+        torch.ops.load_library(OPS_PATH)
+        _ops = torch.ops.mace_b200
+        _register_python_side(torch)
+    return _ops
+
+
+def _register_python_side(torch):
+    """Shape functions (FakeTensor / meta) and the autograd formula of the ops that return new tensors."""
+    from torch import library as tl
+
+    @tl.register_fake("mace_b200::conv_tp")
+    def _conv_fake(node_feats, edge_attrs, tp_weights, edge_index, terms, coef, n_out):
+        return node_feats.new_empty((node_feats.shape[0], n_out * 128))
+
+    @tl.register_fake("mace_b200::conv_tp_backward")
+    def _conv_bwd_fake(grad, node_feats, edge_attrs, tp_weights, edge_index, terms, coef, n_out, nx, ny, nw):
+        return (node_feats.new_empty(node_feats.shape), edge_attrs.new_empty(edge_attrs.shape),
+                tp_weights.new_empty(tp_weights.shape))
+
+    @tl.register_fake("mace_b200::pack_halo")
+    def _pack_fake(src, idx):
+        return src.new_empty((idx.shape[0], src.shape[1]))
+
+    def _setup(ctx, inputs, output):
+        node_feats, edge_attrs, tp_weights, edge_index, terms, coef, n_out = inputs
+        ctx.save_for_backward(node_feats, edge_attrs, tp_weights, edge_index, terms, coef)
+        ctx.n_out = n_out
+
+    def _backward(ctx, grad):
+        X, Y, W, ei, terms, coef = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        dX, dY, dW = torch.ops.mace_b200.conv_tp_backward(grad.contiguous(), X, Y, W, ei, terms, coef, ctx.n_out,
+                                                          bool(need[0]), bool(need[1]), bool(need[2]))
+        return (dX if need[0] else None, dY if need[1] else None, dW if need[2] else None, None, None, None, None)
+
+    tl.register_autograd("mace_b200::conv_tp", _backward, setup_context=_setup)
 
 
 def exported_symbols():

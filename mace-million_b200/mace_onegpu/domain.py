@@ -157,43 +157,48 @@ class HaloExchange:
             self._bufs[key] = b
         return b[:n]
 
-    def _pack(self, src, idx, out):
+    def _pack(self, src, idx, out=None):
+        """Rows src[idx] (into `out` when given, else a new buffer)."""
         if src.is_cuda:
             from . import _native as N
 
+            if out is None:
+                return N.ops().pack_halo(src, idx)
             st = torch.cuda.current_stream(src.device).cuda_stream
             N.check(N.lib().mace_b200_pack_rows(N.ptr(src), N.ptr(idx), idx.numel(), src.shape[1], N.ptr(out), st),
                     "pack_rows")
-        else:
-            out.copy_(src[idx.long()])
+            return out
+        if out is None:
+            return src[idx.long()]
+        out.copy_(src[idx.long()])
+        return out
 
     def _unpack_add(self, buf, idx, dst):
         if dst.is_cuda:
             from . import _native as N
 
-            st = torch.cuda.current_stream(dst.device).cuda_stream
-            N.check(N.lib().mace_b200_unpack_add_rows(N.ptr(buf), N.ptr(idx), idx.numel(), dst.shape[1], N.ptr(dst),
-                                                      st), "unpack_add_rows")
+            N.ops().unpack_halo_add(dst, buf, idx)
         else:
             dst.index_add_(0, idx.long(), buf)
 
     def forward(self, H):
         """H [nt, D]: ghost rows <- owner rows (in place)."""
         dist = self.dist
-        D = H.shape[1]
         ops = []
+        self._sent = []
         for p, idx in self.send.items():
             if p == self.rank:
                 g0, g1 = self.recv[p]
                 self._pack(H, idx, H[self.nl + g0:self.nl + g1])
                 continue
-            buf = self._buf(("f", p), idx.numel(), D, H.dtype)
-            self._pack(H, idx, buf)
+            buf = self._pack(H, idx)
+            self._sent.append(buf)                      # alive until the grouped send completes
             ops.append(dist.P2POp(dist.isend, buf, p, group=self.group))
         for o, (g0, g1) in self.recv.items():
             if o != self.rank:
                 ops.append(dist.P2POp(dist.irecv, H[self.nl + g0:self.nl + g1], o, group=self.group))
         self._run(ops)
+        self._sent = []
 
     def reverse(self, G):
         """G [nt, D]: owner rows += ghost rows (ghost rows left as they are)."""

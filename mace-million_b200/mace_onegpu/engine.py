@@ -538,7 +538,7 @@ class ThreePassEngine:
                 io = self._io
                 io.wait_stream(cur)
             if deferred:
-                L = N.lib()
+                ops = N.ops()
                 h_pi, h_pj, h_rij = plan.host_src
                 waits = self._events("wait", nch)
                 with torch.cuda.stream(io):
@@ -550,9 +550,8 @@ class ThreePassEngine:
                         plan.pi[e0:e1].copy_(h_pi[e0:e1], non_blocking=True)
                         plan.pj[e0:e1].copy_(h_pj[e0:e1], non_blocking=True)
                         plan.rij[e0:e1].copy_(h_rij[e0:e1], non_blocking=True)
-                        N.check(L.mace_b200_csr_rows(N.ptr(plan.pi), e0, e1, int(plan.bounds[k]),
-                                                     int(plan.bounds[k + 1]), N.ptr(plan.rowptr), N.ptr(b["status"]),
-                                                     io.cuda_stream), "csr_rows")
+                        ops.csr_rows(plan.pi, e0, e1, int(plan.bounds[k]), int(plan.bounds[k + 1]), plan.rowptr,
+                                     b["status"])
                         waits[k].record(io)
                     if self.pass_timing:
                         self._h2d_marks[1].record(io)

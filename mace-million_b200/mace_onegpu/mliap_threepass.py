@@ -20,6 +20,8 @@ import time
 
 import torch
 
+from . import _native as N
+
 try:
     from lammps.mliap.mliap_unified_abc import MLIAPUnified
 except ImportError:  # pragma: no cover - LAMMPS is not part of this package
@@ -141,11 +143,9 @@ class ThreePassMLIAP(MLIAPUnified):
 
         eat, PF = eng.evaluate(plan, fwd if nt > nl else None, rev if nt > nl else None, host_pf=hbuf)
         fmax = eng.fmax
-        # force guard (mliap_threepass.py:595-601)
-        if not (bool(torch.isfinite(eat).all()) and fmax == fmax and fmax < self._fmax_abort):
-            raise RuntimeError(f"ThreePassMLIAP guard: non-finite or absurd output at call {self.step} "
-                               f"(max |pair force| = {fmax:.3e} eV/A, limit {self._fmax_abort:g}); aborting before LAMMPS "
-                               f"integrates it. The model is probably extrapolating (check the trajectory / training data).")
+        # force guard (mliap_threepass.py:595-601): torch.ops.mace_b200.guard raises RuntimeError on non-finite
+        # energies or a pair-force maximum that is non-finite or not below MACE3P_FMAX_ABORT
+        N.ops().guard(eat, float(fmax), float(self._fmax_abort), int(self.step))
         torch.as_tensor(data.eatoms).copy_(eat)
         data.energy = float(eat.sum())
         data.update_pair_forces_gpu(hbuf if eng.host_pf_written else PF)

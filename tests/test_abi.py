@@ -44,3 +44,28 @@ def test_hostio_cpulist_parsing():
 
     assert hostio._parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
     assert hostio._parse_cpulist("") == set()
+
+
+def test_custom_ops_register():
+    """torch.ops.mace_b200: every custom op over the C ABI is registered with a schema (TORCH_LIBRARY), tensors and
+    int64 / double / bool scalars only."""
+    ops = N.ops()
+    for name in N.OPS:
+        schema = getattr(ops, name).default._schema
+        assert schema.name == f"mace_b200::{name}"
+        for arg in schema.arguments:
+            assert str(arg.type) in ("Tensor", "Optional[Tensor]", "int", "float", "bool"), (name, arg)
+
+
+def test_custom_op_errors_raise_runtime_error():
+    """A failed check inside an op (TORCH_CHECK in the C++ wrapper) arrives in Python as RuntimeError with the
+    reference's guard message (mliap_threepass.py:595-601), also for host tensors."""
+    import pytest
+    import torch
+
+    ops = N.ops()
+    ops.guard(torch.ones(4, dtype=torch.float64), 1.0, 100.0, 1)
+    with pytest.raises(RuntimeError, match="non-finite or absurd output at call 2"):
+        ops.guard(torch.ones(4, dtype=torch.float64), 250.0, 100.0, 2)
+    with pytest.raises(RuntimeError, match="non-finite or absurd output"):
+        ops.guard(torch.tensor([1.0, float("nan")], dtype=torch.float64), 1.0, 100.0, 3)
