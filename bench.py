@@ -40,6 +40,8 @@ CONFIGS = {
     "water_24k": dict(kind="water", n=20, seed=0, model_seed=0, desc="24,000-atom water box (20^3 H2O)"),
     "water_192": dict(kind="water", n=4, seed=0, model_seed=0, desc="192-atom water box (4^3 H2O)"),
     "alloy_432k": dict(kind="alloy", n=60, seed=0, model_seed=1, desc="432,000-atom 16-element bcc alloy"),
+    "water_8m": dict(kind="water", n=140, seed=0, model_seed=0,
+                     desc="8,232,000-atom water box on one GPU (140^3 H2O, BASELINE config 5's box): memory scaling"),
 }
 # Algorithmic FLOPs per edge of each edge kernel, counted from the algorithm (C = 128 channels, 86 / 16 CG terms,
 # 10 / 4 paths, D = 1280 / 512 spline columns at 8 flops each): forward 8 D + 2 C T + C nW, layer-2 backward
@@ -74,6 +76,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-replica-check", action="store_true", help="multi-GPU: skip the single-GPU comparison")
+    ap.add_argument("--md-steps", type=int, default=10, help="single GPU: MD steps timed after the bench (0: none)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="multi-GPU: run the halo exchanges between whole passes instead of overlapping them with "
+                         "interior chunks")
     ap.add_argument("--cpu-sample", type=int, default=6, help="water molecules per box edge of the CPU sample")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--skin", type=float, default=2.0, help="ghost shell = r_max + skin (multi-GPU)")
@@ -203,6 +209,38 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ MD
+def md_timing(args, cfg, m, eng, dev):
+    """Velocity-Verlet MD on the configuration's box (BASELINE config 3's schedule: dt 1 fs, Verlet skin 2 A,
+    Maxwell-Boltzmann velocities at 300 K; mace_onegpu/md.py), timed over args.md_steps steps with CUDA events after
+    the force-evaluation timing.  The random-init model (energy scale 100) heats water within tens of fs, so this
+    is a timing figure of the MD loop (force evaluation, Verlet-list filter / rebuild, integration), not physics."""
+    import torch
+
+    from mace_onegpu import structures as S
+    from mace_onegpu.md import VelocityVerlet
+
+    pos, Z, box = build_structure(cfg)
+    cols = S.species_columns(Z, m.arch.atomic_numbers)
+    vel = S.maxwell_boltzmann(Z, 300.0, seed=0)
+    md = VelocityVerlet(eng, pos, box, cols, Z, vel, dt=1.0, skin=2.0)
+    md.step()                                           # warm-up step
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.md_steps):
+        md.step()
+    t1.record()
+    torch.cuda.synchronize()
+    sps = args.md_steps / (t0.elapsed_time(t1) * 1e-3)
+    out = {"md_ns_per_day": sps * 1.0 * 86400 / 1e6, "steps_per_s": sps, "steps": args.md_steps, "dt_fs": 1.0,
+           "skin_A": 2.0, "neighbour_rebuilds": md.rebuilds,
+           "note": "random-init model: a timing figure of the MD loop, not a physical trajectory"}
+    del md
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------------------------------------ replica check
 def replica_check(args, cfg, m, dev, eng, step, hx, gid, n, nt, pi, pj, n_cell):
     """Multi-GPU correctness inside every scaling run.  Each rank evaluates the single-GPU box (the weak-scaling
@@ -306,7 +344,9 @@ def main():
         pi, pj, rij = NB.neighbor_list_open(p, n, m.arch.r_max, device=dev)
         cols = cols_all[torch.as_tensor(gid)]
         hx = DM.HaloExchange(dec, rank, dev)
-        parallelism = f"domain {grid[0]}x{grid[1]}x{grid[2]}, NCCL halo exchange, ghost shell {m.arch.r_max + args.skin:g} A"
+        parallelism = (f"domain {grid[0]}x{grid[1]}x{grid[2]}, NCCL halo exchange "
+                       f"({'between passes' if args.no_overlap else 'overlapped with interior chunks'}), "
+                       f"ghost shell {m.arch.r_max + args.skin:g} A, {hx.n_interior} interior atoms on rank 0")
     P = int(pi.numel())
     elems = cols.to(dev)
     eng = ThreePassEngine(m, sorted(set(cols_all.tolist())), chunk=args.chunk, device=dev)
@@ -319,7 +359,9 @@ def main():
         plan = eng.plan(pi, pj, rij, elems, n, nt)
         if hx is None:
             return eng.evaluate(plan)
-        return eng.evaluate(plan, hx.forward, hx.reverse)
+        if args.no_overlap:
+            return eng.evaluate(plan, hx.forward, hx.reverse)
+        return eng.evaluate(plan, halo=hx)
 
     # the per-kind breakdown comes from the last warm-up step; inside the timed region only the roofline kernel is
     # recorded (every recorded launch adds two event records to the stream: all kinds cost ~1% of the step time)
@@ -402,6 +444,10 @@ def main():
         e2e["breakdown_s"] = {k: round(v, 5) for k, v in mli._eng.pass_times().items()}
         mli._eng.pass_timing = False
 
+    md = None
+    if world == 1 and args.md_steps > 0:
+        md = md_timing(args, cfg, m, eng, dev)
+
     replica = None
     if world > 1 and not args.no_replica_check:
         replica = replica_check(args, cfg, m, dev, eng, step, hx, gid, n, nt, pi, pj, n_cell)
@@ -438,7 +484,7 @@ def main():
                              "peak_source": "FFMA issue ceiling measured in this run (mace_b200_ffma_peak)",
                              "flops_per_edge": fpe[dom]},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks, "kernels": kinds,
-                "replica_check": replica}
+                "replica_check": replica, "md": md}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

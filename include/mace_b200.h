@@ -272,6 +272,18 @@ int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev, void* stream);
 int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* stream);
 int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* stream);
 int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev, void* stream);
+/* The same passes split so that a caller can overlap the halo exchanges with interior work (the reference leaves
+ * the exchanges to LAMMPS between whole passes, mliap_threepass.py:522,556):
+ * pass_a_chunks / pass_b_chunks / pass_c_chunks run chunks [c0, c1) (chunk k = receivers [k chunk, (k+1) chunk));
+ *   pass_a_chunks adds the R1 energies of those chunks' receivers; pass_b_chunks neither zeroes PF nor folds GX2.
+ * x2_rows: X2 = linear_up(H1) and zeroed G1 / GX2 for rows [r0, r1).
+ * fold_g1: G1[r0:r1] += linear_up^T(GX2[r0:r1]).
+ * pass_a = pass_a_chunks(all); x2_all = x2_rows(0, nt); pass_b = zero PF, pass_b_chunks(all), fold_g1(0, nt). */
+int mace_b200_pass_a_chunks(const mb_model_t* m, const mb_eval_t* ev, int32_t c0, int32_t c1, void* stream);
+int mace_b200_x2_rows(const mb_model_t* m, const mb_eval_t* ev, int32_t r0, int32_t r1, void* stream);
+int mace_b200_pass_b_chunks(const mb_model_t* m, const mb_eval_t* ev, int32_t c0, int32_t c1, void* stream);
+int mace_b200_fold_g1(const mb_model_t* m, const mb_eval_t* ev, int32_t r0, int32_t r1, void* stream);
+int mace_b200_pass_c_chunks(const mb_model_t* m, const mb_eval_t* ev, int32_t c0, int32_t c1, void* stream);
 int mace_b200_finalize(const mb_model_t* m, const mb_eval_t* ev, const int64_t* perm, double* PFd,
                        uint32_t* fmax_bits, void* stream);
 

@@ -210,11 +210,24 @@ static mb_eval_t chunk_view(const mb_eval_t* ev, int a) {
   return v;
 }
 
-extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev_all, void* stream) {
+static int n_chunks(const mb_eval_t* ev) { return (ev->nl + ev->chunk - 1) / ev->chunk; }
+
+static int chunk_range_ok(const mb_eval_t* ev, int c0, int c1, const char* who) {
+  if (c0 < 0 || c1 < c0 || c1 > n_chunks(ev)) {
+    set_error("%s: chunk range [%d, %d) outside [0, %d)", who, c0, c1, n_chunks(ev));
+    return MB_E_ARG;
+  }
+  return 0;
+}
+
+extern "C" int mace_b200_pass_a_chunks(const mb_model_t* m, const mb_eval_t* ev_all, int32_t c0, int32_t c1,
+                                       void* stream) {
   RC(check_pass_args(m, ev_all, "pass_a"));
+  RC(chunk_range_ok(ev_all, c0, c1, "pass_a"));
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C;
-  for (int a = 0, ci = 0; a < ev_all->nl; a += ev_all->chunk, ++ci) {
+  for (int ci = c0; ci < c1; ++ci) {
+    const int a = ci * ev_all->chunk;
     const mb_eval_t view = chunk_view(ev_all, a);
     const mb_eval_t* ev = &view;
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
@@ -232,36 +245,52 @@ extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev_all, vo
              ev->H1 + (size_t)a * 4 * C, 4 * C, kOffL[l], 2 * l + 1, nullptr, nC, nullptr, 0));
     RC(gb.launch());
   }
-  return readout1(m, ev_all->H1, ev_all->eat, ev_all->nl, st);
+  const int r0 = c0 * ev_all->chunk, r1 = min(c1 * ev_all->chunk, ev_all->nl);
+  return r1 > r0 ? readout1(m, ev_all->H1 + (size_t)r0 * 4 * C, ev_all->eat + r0, r1 - r0, st) : 0;
 }
 
-extern "C" int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
-  RC(check_pass_args(m, ev, "x2_all"));
+extern "C" int mace_b200_pass_a(const mb_model_t* m, const mb_eval_t* ev_all, void* stream) {
+  RC(check_pass_args(m, ev_all, "pass_a"));
+  return mace_b200_pass_a_chunks(m, ev_all, 0, n_chunks(ev_all), stream);
+}
+
+extern "C" int mace_b200_x2_rows(const mb_model_t* m, const mb_eval_t* ev, int32_t r0, int32_t r1, void* stream) {
+  RC(check_pass_args(m, ev, "x2_rows"));
+  if (r0 < 0 || r1 < r0 || r1 > ev->nt) {
+    set_error("x2_rows: rows [%d, %d) outside [0, %d)", r0, r1, ev->nt);
+    return MB_E_ARG;
+  }
+  if (r1 == r0) return 0;
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C;
-  const size_t bytes = (size_t)ev->nt * 4 * C * sizeof(float);
-  if (cudaMemsetAsync(ev->G1, 0, bytes, st) != cudaSuccess || cudaMemsetAsync(ev->GX2, 0, bytes, st) != cudaSuccess) {
-    set_error("x2_all: cudaMemsetAsync failed");
+  const size_t off = (size_t)r0 * 4 * C, bytes = (size_t)(r1 - r0) * 4 * C * sizeof(float);
+  if (cudaMemsetAsync(ev->G1 + off, 0, bytes, st) != cudaSuccess ||
+      cudaMemsetAsync(ev->GX2 + off, 0, bytes, st) != cudaSuccess) {
+    set_error("x2_rows: cudaMemsetAsync failed");
     return MB_E_CUDA;
   }
   GemmBatch gb(use_tc(m), ev->status, st);
   for (int l = 0; l < 2; ++l)
-    RC(add(gb, {m->Wup2, m->Wup2_tc, 2 * C * C}, (size_t)l * C * C, ev->H1, 4 * C, &kOffL[l], 1, ev->X2, 4 * C,
-           kOffL[l], 2 * l + 1, nullptr, ev->nt, nullptr, 0));
+    RC(add(gb, {m->Wup2, m->Wup2_tc, 2 * C * C}, (size_t)l * C * C, ev->H1 + off, 4 * C, &kOffL[l], 1,
+           ev->X2 + off, 4 * C, kOffL[l], 2 * l + 1, nullptr, r1 - r0, nullptr, 0));
   return gb.launch();
 }
 
-extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+extern "C" int mace_b200_x2_all(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+  RC(check_pass_args(m, ev, "x2_all"));
+  return mace_b200_x2_rows(m, ev, 0, ev->nt, stream);
+}
+
+extern "C" int mace_b200_pass_b_chunks(const mb_model_t* m, const mb_eval_t* ev, int32_t c0, int32_t c1,
+                                       void* stream) {
   RC(check_pass_args(m, ev, "pass_b"));
+  RC(chunk_range_ok(ev, c0, c1, "pass_b"));
   cudaStream_t st = (cudaStream_t)stream;
   const int C = MB_C, S = m->S;
   const bool tc = use_tc(m);
-  if (ev->P > 0 && cudaMemsetAsync(ev->PF, 0, (size_t)ev->P * 3 * sizeof(float), st) != cudaSuccess) {
-    set_error("pass_b: cudaMemsetAsync(PF) failed");
-    return MB_E_CUDA;
-  }
   const int zero = 0;
-  for (int a = 0, ci = 0; a < ev->nl; a += ev->chunk, ++ci) {
+  for (int ci = c0; ci < c1; ++ci) {
+    const int a = ci * ev->chunk;
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;
     const int32_t* so = ev->spec_off + (size_t)ci * (S + 1);
     TIMED(MB_K_EDGE_L2_FWD, mace_b200_edge_l2_fwd(m, ev, a, b, st));
@@ -309,15 +338,45 @@ extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* 
     }
     TIMED(MB_K_EDGE_L2_BWD, mace_b200_edge_l2_bwd(m, ev, a, b, st));
   }
-  GemmBatch gb(tc, ev->status, st);
+  return 0;
+}
+
+extern "C" int mace_b200_fold_g1(const mb_model_t* m, const mb_eval_t* ev, int32_t r0, int32_t r1, void* stream) {
+  RC(check_pass_args(m, ev, "fold_g1"));
+  if (r0 < 0 || r1 < r0 || r1 > ev->nt) {
+    set_error("fold_g1: rows [%d, %d) outside [0, %d)", r0, r1, ev->nt);
+    return MB_E_ARG;
+  }
+  if (r1 == r0) return 0;
+  const int C = MB_C;
+  const size_t off = (size_t)r0 * 4 * C;
+  GemmBatch gb(use_tc(m), ev->status, (cudaStream_t)stream);
   for (int l = 0; l < 2; ++l)
-    RC(add(gb, {m->Wup2T, m->Wup2T_tc, 2 * C * C}, (size_t)l * C * C, ev->GX2, 4 * C, &kOffL[l], 1, ev->G1, 4 * C,
-           kOffL[l], 2 * l + 1, nullptr, ev->nt, nullptr, 1));
+    RC(add(gb, {m->Wup2T, m->Wup2T_tc, 2 * C * C}, (size_t)l * C * C, ev->GX2 + off, 4 * C, &kOffL[l], 1,
+           ev->G1 + off, 4 * C, kOffL[l], 2 * l + 1, nullptr, r1 - r0, nullptr, 1));
   return gb.launch();
 }
 
+extern "C" int mace_b200_pass_b(const mb_model_t* m, const mb_eval_t* ev, void* stream) {
+  RC(check_pass_args(m, ev, "pass_b"));
+  if (ev->P > 0 && cudaMemsetAsync(ev->PF, 0, (size_t)ev->P * 3 * sizeof(float), (cudaStream_t)stream) != cudaSuccess) {
+    set_error("pass_b: cudaMemsetAsync(PF) failed");
+    return MB_E_CUDA;
+  }
+  RC(mace_b200_pass_b_chunks(m, ev, 0, n_chunks(ev), stream));
+  return mace_b200_fold_g1(m, ev, 0, ev->nt, stream);
+}
+
+
 extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev_all, void* stream) {
   RC(check_pass_args(m, ev_all, "pass_c"));
+  return mace_b200_pass_c_chunks(m, ev_all, 0, n_chunks(ev_all), stream);
+}
+
+extern "C" int mace_b200_pass_c_chunks(const mb_model_t* m, const mb_eval_t* ev_all, int32_t c0, int32_t c1,
+                                       void* stream) {
+  RC(check_pass_args(m, ev_all, "pass_c"));
+  RC(chunk_range_ok(ev_all, c0, c1, "pass_c"));
   if (ev_all->done_ev && (!ev_all->pf_out || !ev_all->fmax_bits)) {
     set_error("pass_c: done_ev needs pf_out and fmax_bits");
     return MB_E_ARG;
@@ -327,7 +386,8 @@ extern "C" int mace_b200_pass_c(const mb_model_t* m, const mb_eval_t* ev_all, vo
   const bool tc = use_tc(m);
   const bool cached = ev_all->x1_cache && ev_all->rho1_cache;
   static const int offs[4] = {0, 1, 4, 9};
-  for (int a = 0, ci = 0; a < ev_all->nl; a += ev_all->chunk, ++ci) {
+  for (int ci = c0; ci < c1; ++ci) {
+    const int a = ci * ev_all->chunk;
     const mb_eval_t view = chunk_view(ev_all, a);
     const mb_eval_t* ev = &view;
     const int b = min(a + ev->chunk, ev->nl), nC = b - a;

@@ -76,6 +76,11 @@ _SIGS = {
     "mace_b200_pass_b": (c_i32, [c_vp, c_vp, c_vp]),
     "mace_b200_pass_c": (c_i32, [c_vp, c_vp, c_vp]),
     "mace_b200_finalize": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mace_b200_pass_a_chunks": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_x2_rows": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_pass_b_chunks": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_fold_g1": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "mace_b200_pass_c_chunks": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
     "mace_b200_pack_rows": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp]),
     "mace_b200_unpack_add_rows": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp]),
     "mace_b200_nbr_count": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_f64, c_vp, c_vp]),

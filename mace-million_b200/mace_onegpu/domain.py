@@ -54,13 +54,6 @@ class Decomposition:
         cell = np.minimum((pos / w).astype(np.int64), grid - 1)
         owner = (cell[:, 0] * grid[1] + cell[:, 1]) * grid[2] + cell[:, 2]
         self.owner = owner
-        order = np.argsort(owner, kind="stable")
-        counts = np.bincount(owner, minlength=self.nranks)
-        self.local = np.split(order, np.cumsum(counts)[:-1])          # global indices of each rank's atoms
-        local_index = np.empty(len(pos), dtype=np.int64)
-        for r, idx in enumerate(self.local):
-            local_index[idx] = np.arange(len(idx))
-        self.local_index = local_index
         # ghost entries (rank, global atom, image shift) over all ranks
         entries = []
         for s in itertools.product((-1, 0, 1), repeat=3):
@@ -93,6 +86,20 @@ class Decomposition:
                     entries.append(np.stack([rank[keep], ii[keep], np.full(int(keep.sum()), code)], 1))
         E = np.concatenate(entries, 0) if entries else np.zeros((0, 3), dtype=np.int64)
         E = np.unique(E, axis=0)                                   # (rank, atom, image) unique
+        # each rank's atoms: interior atoms (a ghost on no rank, so no ghost lies within r_ghost > r_max of them)
+        # first, boundary atoms (sent to some rank) last, each group in global order.  Interior receivers have no
+        # ghost senders, so their chunks can run while a halo exchange is in flight.
+        boundary = np.zeros(len(pos), dtype=bool)
+        boundary[E[:, 1]] = True
+        key = owner * 2 + boundary
+        order = np.argsort(key, kind="stable")
+        counts = np.bincount(owner, minlength=self.nranks)
+        self.local = np.split(order, np.cumsum(counts)[:-1])          # global indices of each rank's atoms
+        self.n_interior = [int((~boundary[idx]).sum()) for idx in self.local]
+        local_index = np.empty(len(pos), dtype=np.int64)
+        for r, idx in enumerate(self.local):
+            local_index[idx] = np.arange(len(idx))
+        self.local_index = local_index
         self.ghost = []
         for r in range(self.nranks):
             er = E[E[:, 0] == r]
@@ -149,6 +156,8 @@ class HaloExchange:
                 self.send[p] = torch.as_tensor(idx, dtype=torch.int32, device=self.device)
         self.bytes_fwd = 0
         self._bufs = {}
+        self._pending = []
+        self.n_interior = dec.n_interior[rank]      # local atoms [0, n_interior) have no ghost neighbours
 
     def _buf(self, key, n, D, dtype):
         b = self._bufs.get(key)
@@ -202,6 +211,12 @@ class HaloExchange:
 
     def reverse(self, G):
         """G [nt, D]: owner rows += ghost rows (ghost rows left as they are)."""
+        self.reverse_comm(G)
+        self.reverse_unpack(G)
+
+    def reverse_comm(self, G):
+        """The communication half of reverse(): ghost rows go to their owners, the owners' received blocks wait in
+        buffers (and the rank's own periodic images in a copy) until reverse_unpack(G) adds them."""
         dist = self.dist
         D = G.shape[1]
         ops, pending = [], []
@@ -218,9 +233,17 @@ class HaloExchange:
         self._run(ops)
         if self.rank in self.send:
             g0, g1 = self.recv[self.rank]
-            self._unpack_add(G[self.nl + g0:self.nl + g1].clone(), self.send[self.rank], G)
-        for buf, idx in pending:
+            pending.append((G[self.nl + g0:self.nl + g1].clone(), self.send[self.rank]))
+        self._pending = pending
+
+    def reverse_unpack(self, G):
+        """Adds the blocks reverse_comm(G) received onto their owner rows (on the current stream, which may differ
+        from the one reverse_comm ran on: the buffers are recorded on it before they are released)."""
+        for buf, idx in self._pending:
             self._unpack_add(buf, idx, G)
+            if buf.is_cuda:
+                buf.record_stream(torch.cuda.current_stream(buf.device))
+        self._pending = []
 
     def _run(self, ops):
         if not ops:

@@ -477,6 +477,62 @@ class ThreePassEngine:
         mark(6)
         return PFd, fbits
 
+    def _run_overlap(self, plan, ev, b, halo):
+        """The evaluation with both halo exchanges overlapped with interior chunks.  Chunk k holds local atoms
+        [k chunk, (k + 1) chunk); chunks [0, kI) hold interior atoms only (no ghost senders, and no rank receives
+        their rows), the rest hold the boundary atoms.  Main stream / side stream:
+            pass A boundary chunks                  -> side: H1 forward exchange
+            pass A interior chunks, X2 of local rows, pass B interior chunks
+            (wait forward) X2 of ghost rows, pass B boundary chunks, fold of the ghost rows of G1
+                                                    -> side: G1 reverse exchange (communication)
+            fold of the local rows of G1, pass C interior chunks
+            (wait reverse) received ghost rows added onto their owners, pass C boundary chunks, finalize.
+        Every rank issues the same exchanges in the same order."""
+        L = N.lib()
+        m = N.byref(self.fm.struct)
+        evp = N.byref(ev)
+        cur = torch.cuda.current_stream(self.device)
+        st = cur.cuda_stream
+        if getattr(self, "_halo_stream", None) is None:
+            self._halo_stream = torch.cuda.Stream(self.device)
+        side = self._halo_stream
+        nl, nt, nch = plan.nl, plan.nt, plan.n_chunks
+        kI = min(int(halo.n_interior) // self.chunk, nch)
+        self._marks_valid = False
+        b["eat"].zero_()
+        PFd = self._get("PFd", (plan.P, 3), torch.float64)
+        fbits = self._get("fmax", (1,), torch.int32)
+        fbits.zero_()
+        H1 = b["H1"].view(nt, 4 * C)
+        G1 = b["G1"].view(nt, 4 * C)
+        e_a, e_fwd, e_b, e_rev = (torch.cuda.Event() for _ in range(4))
+        N.check(L.mace_b200_pass_a_chunks(m, evp, kI, nch, st), "pass_a")
+        e_a.record(cur)
+        with torch.cuda.stream(side):
+            side.wait_event(e_a)
+            halo.forward(H1)
+            e_fwd.record(side)
+        N.check(L.mace_b200_pass_a_chunks(m, evp, 0, kI, st), "pass_a")
+        N.check(L.mace_b200_x2_rows(m, evp, 0, nl, st), "x2_rows")
+        b["PF"].zero_()
+        N.check(L.mace_b200_pass_b_chunks(m, evp, 0, kI, st), "pass_b")
+        cur.wait_event(e_fwd)
+        N.check(L.mace_b200_x2_rows(m, evp, nl, nt, st), "x2_rows")
+        N.check(L.mace_b200_pass_b_chunks(m, evp, kI, nch, st), "pass_b")
+        N.check(L.mace_b200_fold_g1(m, evp, nl, nt, st), "fold_g1")
+        e_b.record(cur)
+        with torch.cuda.stream(side):
+            side.wait_event(e_b)
+            halo.reverse_comm(G1)
+            e_rev.record(side)
+        N.check(L.mace_b200_fold_g1(m, evp, 0, nl, st), "fold_g1")
+        N.check(L.mace_b200_pass_c_chunks(m, evp, 0, kI, st), "pass_c")
+        cur.wait_event(e_rev)
+        halo.reverse_unpack(G1)
+        N.check(L.mace_b200_pass_c_chunks(m, evp, kI, nch, st), "pass_c")
+        N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
+        return PFd, fbits
+
     _PASSES = ("A", "xchg_fwd", "B", "xchg_rev", "C", "finalize")
 
     def _pass_marks(self):
@@ -510,11 +566,15 @@ class ThreePassEngine:
         return evs[:n]
 
     def evaluate(self, plan: Plan, forward_exchange=None, reverse_exchange=None, check: bool = True,
-                 graph: bool | None = None, host_pf=None):
+                 graph: bool | None = None, host_pf=None, halo=None):
         """(eatoms fp64 [nl], pair forces dE/drij fp64 [P, 3] in the caller's pair order) on the device.
         forward_exchange(H1 [nt, 512]) fills ghost rows from their owners; reverse_exchange(G1 [nt, 512]) adds
         ghost rows onto their owners (both in place; None when nt == nl).  graph=True (or engine.graphs) replays
         the whole evaluation as one captured CUDA graph when there is no exchange to run between the passes.
+
+        halo (instead of the two callbacks): an exchange object with forward(H), reverse_comm(G), reverse_unpack(G)
+        and n_interior, whose local atoms [0, n_interior) have no ghost neighbours (domain.HaloExchange).  The
+        exchanges then run on a side stream, overlapped with interior work (_run_overlap).
 
         Host I/O overlap: a plan whose senders / vectors are in pinned host memory (Plan.host_src) gets them copied
         chunk by chunk on a side stream, pass A waiting per chunk; with host_pf (pinned fp64 [P, 3]) and
@@ -566,7 +626,10 @@ class ThreePassEngine:
                 arr2 = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in done])
                 keep.append(arr2)
                 ev.done_ev = N.ctypes.addressof(arr2)
-            PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange, zero_status=False)
+            if halo is not None and plan.nt > plan.nl:
+                PFd, fbits = self._run_overlap(plan, ev, b, halo)
+            else:
+                PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange, zero_status=False)
             if out_host:
                 with torch.cuda.stream(io):
                     for k in range(nch):

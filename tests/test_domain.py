@@ -39,6 +39,26 @@ def test_ghosts_reproduce_minimum_image_pairs(grid):
     assert got == ref
 
 
+@pytest.mark.parametrize("grid", [(2, 1, 1), (1, 2, 1)])
+def test_interior_atoms_first_have_no_ghost_neighbours(grid):
+    """Each rank's local atoms are ordered interior first: receivers [0, n_interior) have only local senders and are
+    in no rank's ghost list, so their chunks may run while a halo exchange is in flight (engine._run_overlap).  The
+    box leaves every domain wider than twice the 8 A ghost shell, so that it has interior atoms."""
+    pos, Z, box = S.water_box(*((14, 8, 8) if grid[0] == 2 else (8, 14, 8)), seed=1)
+    r = 6.0
+    dec = D.Decomposition(pos, box, grid, r + 2.0)
+    ghosts_of = {int(a) for g in dec.ghost for a in g[:, 0]}
+    for rank in range(dec.nranks):
+        p, gid, nl = dec.rank_atoms(rank)
+        ni = dec.n_interior[rank]
+        assert 0 < ni < nl
+        assert not ({int(a) for a in gid[:ni]} & ghosts_of)
+        assert {int(a) for a in gid[ni:nl]} <= ghosts_of
+        qi, qj, _ = NB.neighbor_list_open(p, nl, r)
+        inner = qi < ni
+        assert bool((qj[inner] < nl).all())
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

@@ -1,7 +1,9 @@
 """Multi-GPU parity: the three-pass evaluation split over 2 GPUs by spatial domains (explicit ghosts, H1 forward /
-G1 reverse halo exchange over NCCL) reproduces the single-process fp64 oracle.  Needs >= 2 GPUs (skipped otherwise);
+G1 reverse halo exchange over NCCL, between whole passes or overlapped with interior chunks on a side stream)
+reproduces the single-process fp64 oracle.  Needs >= 2 GPUs (skipped otherwise);
 ranks run as child processes; NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout."""
 import dataclasses
+import functools
 import os
 import queue
 import socket
@@ -28,7 +30,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, grid, out_q):
+def _worker(rank, world, port, grid, out_q, overlap):
     import datetime
 
     import torch.distributed as dist
@@ -42,15 +44,19 @@ def _worker(rank, world, port, grid, out_q):
                             timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
         mdl = M.default_model(0)
-        pos, Z, box = S.water_box(8, 4, 4, seed=2)
+        pos, Z, box = S.water_box(16, 8, 8, seed=2)
         cols = S.species_columns(Z, mdl.arch.atomic_numbers)
         dec = D.Decomposition(pos, box, grid, mdl.arch.r_max + 2.0)
         p, gid, nl = dec.rank_atoms(rank)
         pi, pj, rij = NB.neighbor_list_open(p, nl, mdl.arch.r_max, device=dev)
-        eng = ThreePassEngine(mdl, sorted(set(cols.tolist())), chunk=100, device=dev)
+        eng = ThreePassEngine(mdl, sorted(set(cols.tolist())), chunk=32, device=dev)
         hx = D.HaloExchange(dec, rank, dev)
         plan = eng.plan(pi, pj, rij, torch.as_tensor(cols[gid]), nl, len(gid))
-        eat, pf = eng.evaluate(plan, hx.forward, hx.reverse)
+        if overlap:
+            assert hx.n_interior >= 32                   # at least one interior chunk runs under each exchange
+            eat, pf = eng.evaluate(plan, halo=hx)
+        else:
+            eat, pf = eng.evaluate(plan, hx.forward, hx.reverse)
         torch.cuda.synchronize()
         n = len(Z)
         E = torch.zeros(n, dtype=torch.float64, device=dev)
@@ -67,15 +73,28 @@ def _worker(rank, world, port, grid, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_domain_decomposition_matches_oracle():
+@functools.lru_cache(maxsize=1)
+def _oracle():
     from oracle import mace_ref
+
+    mdl = M.default_model(0)
+    pos, Z, box = S.water_box(16, 8, 8, seed=2)
+    cols = S.species_columns(Z, mdl.arch.atomic_numbers)
+    pi, pj, rij = NB.neighbor_list(pos, box, mdl.arch.r_max)
+    ref = mace_ref.MaceRef(mdl.params(), dataclasses.asdict(mdl.arch), spline_knots=512)
+    e0, pf0 = ref.three_pass(pi, pj, rij, cols, len(Z), 512)
+    return e0, mace_ref.atom_forces(pi, pj, pf0, len(Z)).numpy()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("overlap", [False, True], ids=["between-passes", "overlapped"])
+def test_two_gpu_domain_decomposition_matches_oracle(overlap):
 
     grid, world = (2, 1, 1), 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, grid, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, grid, q, overlap)) for r in range(world)]
     for p_ in procs:
         p_.start()
     t0 = time.time()
@@ -89,12 +108,6 @@ def test_two_gpu_domain_decomposition_matches_oracle():
     for p_ in procs:
         p_.join(timeout=120)
         assert p_.exitcode == 0
-    mdl = M.default_model(0)
-    pos, Z, box = S.water_box(8, 4, 4, seed=2)
-    cols = S.species_columns(Z, mdl.arch.atomic_numbers)
-    pi, pj, rij = NB.neighbor_list(pos, box, mdl.arch.r_max)
-    ref = mace_ref.MaceRef(mdl.params(), dataclasses.asdict(mdl.arch), spline_knots=512)
-    e0, pf0 = ref.three_pass(pi, pj, rij, cols, len(Z), 128)
-    F0 = mace_ref.atom_forces(pi, pj, pf0, len(Z)).numpy()
+    e0, F0 = _oracle()
     assert np.abs(E - e0.numpy()).max() < 1e-5
     assert np.abs(F - F0).max() < 1e-3
