@@ -474,7 +474,8 @@ def main():
                            "parallelism": parallelism, "gemm": "tcgen05 3xTF32" if eng.fm.use_tc else "SIMT fp32",
                            "layer1": "density projection" if eng.fm.l1_density else "direct",
                            "host_numa_bound": numa,
-                           "l2": "inputs larger than L2 (no flush)", "atom_order": ORDER},
+                           "l2": "inputs larger than L2 (no flush)", "atom_order": ORDER,
+                           "peak_device_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 2)},
                 "roofline": {"bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak,
                              "traffic": TRAFFIC_PER_LAUNCH.get((args.config, args.chunk, dom)),
