@@ -249,6 +249,11 @@ int mace_b200_node_gemm(const float* X, int64_t ldx, const int32_t* xoff, int32_
 int mace_b200_node_gemm_tc(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg, const float* Bt_split,
                            int64_t plane, float* Y, int64_t ldy, int32_t yoff, int32_t mult, const int32_t* order,
                            int32_t n_atoms, const float* rho, int32_t accumulate, uint32_t* status, void* stream);
+/* No counterpart in the reference: test hooks of the tensor-core GEMM on the current device.  wait_ns bounds every
+ * mbarrier wait of k_gemm_tc (default 2 s); skip_one_arrival = 1 makes the next launch lose one producer arrival,
+ * so that its waits expire and it reports MB_ST_TC_TIMEOUT after draining its copies and MMAs and freeing its TMEM
+ * (the error path is exercised without any fault).  Not for production use. */
+int mace_b200_tc_test_hooks(uint64_t wait_ns, int32_t skip_one_arrival);
 
 /* ---------------------------------------------------------------- symmetric contraction
  * Replaces products[k].symmetric_contractions (mace EquivariantProductBasisBlock, correlation 3).

@@ -41,7 +41,17 @@ constexpr int TC_RAW_OFF = TC_STAGES * TC_STAGE_BYTES;
 constexpr int TC_EPI_OFF = TC_RAW_OFF + TC_RAW * TC_RAW_BYTES;
 constexpr int TC_BAR_OFF = TC_EPI_OFF + TC_EPI_BYTES;
 constexpr int TC_SMEM = TC_BAR_OFF + 256 + 1024;           // + barriers / TMEM slot / flag + alignment slack
-constexpr unsigned long long TC_WAIT_LIMIT = 1ull << 26;  // try_wait polls before giving up
+// Every mbarrier wait gives up after g_tc_wait_ns nanoseconds of %globaltimer (default 2 s; a GEMM tile takes
+// microseconds).  mace_b200_tc_test_hooks shortens it and can make one producer arrival go missing, so that a test
+// drives the timeout path (MB_ST_TC_TIMEOUT, drain, TMEM release) without any fault.
+__device__ unsigned long long g_tc_wait_ns = 2000000000ull;
+__device__ int g_tc_skip_arrival = 0;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -102,10 +112,12 @@ __device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-// Bounded wait for the phase with the given parity; returns false when the limit expired.
+// Bounded wait for the phase with the given parity; returns false when g_tc_wait_ns expired (the clock is read every
+// 256 polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  for (unsigned long long it = 0; it < TC_WAIT_LIMIT; ++it) {
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -115,8 +127,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(a), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((it & 255u) == 0u) {
+      const unsigned long long now = globaltimer_ns();
+      if (it == 0)
+        t0 = now;
+      else if (now - t0 > *(volatile unsigned long long*)&g_tc_wait_ns)
+        return false;
+    }
   }
-  return false;
 }
 
 // global -> this CTA's shared memory, completing on an mbarrier transaction count (16-byte aligned, bytes % 16 == 0)
@@ -272,7 +290,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
           *reinterpret_cast<float4*>(st + TC_TILE_BYTES + off) = lo;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(&B.full[s]);
+        // test hook (off unless mace_b200_tc_test_hooks armed it): one arrival of CTA 0's first K block goes missing
+        const bool skip = seq == 0 && p == 0 && blockIdx.x == 0 && *(volatile int*)&g_tc_skip_arrival &&
+                          atomicExch(&g_tc_skip_arrival, 0);
+        if (!skip) mbar_arrive(&B.full[s]);
       }
       if (tile + (int)gridDim.x < n_tiles) rw = tc_row(grp, tile + gridDim.x, p);
     }
@@ -434,6 +455,21 @@ int gemm_group_launch_tc(const GemmGroup& grp0, cudaStream_t st) {
 }  // namespace mb
 
 using namespace mb;
+
+extern "C" int mace_b200_tc_test_hooks(uint64_t wait_ns, int32_t skip_one_arrival) {
+  if (wait_ns == 0) {
+    set_error("tc_test_hooks: wait_ns must be positive");
+    return MB_E_ARG;
+  }
+  const unsigned long long w = wait_ns;
+  const int k = skip_one_arrival ? 1 : 0;
+  if (cudaMemcpyToSymbol(g_tc_wait_ns, &w, sizeof(w)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_tc_skip_arrival, &k, sizeof(k)) != cudaSuccess) {
+    set_error("tc_test_hooks: cudaMemcpyToSymbol failed");
+    return MB_E_CUDA;
+  }
+  return 0;
+}
 
 extern "C" int mace_b200_node_gemm_tc(const float* X, int64_t ldx, const int32_t* xoff, int32_t n_seg,
                                       const float* Bt_split, int64_t plane, float* Y, int64_t ldy, int32_t yoff,

@@ -53,3 +53,34 @@ def test_tc_gemm_matches_simt(mult, xoff, ncomp, yoff, ycomp, n, use_order, use_
     # output scale (TF32 alone would be ~1e-3)
     scale = Ys.abs().max().item()
     assert (Yt - Ys).abs().max().item() <= 1e-5 * scale
+
+
+def test_tc_gemm_timeout_path_reports_and_recovers():
+    """The bounded-wait error path, driven from the host: with one producer arrival withheld (test hook), the
+    kernel's barrier waits expire after 20 ms, it drains its copies and MMAs, frees its TMEM and sets
+    MB_ST_TC_TIMEOUT in the status word; the next launch with the default limit is correct."""
+    L = N.lib()
+    n, xoff = 3000, [0]
+    g = torch.Generator(device="cuda").manual_seed(2)
+    X = torch.randn(n, 1, C, device="cuda", generator=g)
+    B = (torch.randn(1, C, C, device="cuda", generator=g) / np.sqrt(C)).contiguous()
+    Bt = torch.as_tensor(E.tc_planes(B.double().cpu().numpy()), device="cuda").contiguous()
+    st = torch.cuda.current_stream().cuda_stream
+    xo = (N.c_i32 * 4)(0, 0, 0, 0)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    Y = torch.zeros(n, 1, C, device="cuda")
+    try:
+        N.check(L.mace_b200_tc_test_hooks(20_000_000, 1), "tc_test_hooks")
+        N.check(L.mace_b200_node_gemm_tc(N.ptr(X), C, xo, 1, N.ptr(Bt), Bt[0].numel(), N.ptr(Y), C, 0, 1, None, n,
+                                         None, 0, N.ptr(status), st), "gemm_tc")
+        torch.cuda.synchronize()
+        assert int(status.item()) & 32                       # MB_ST_TC_TIMEOUT
+    finally:
+        N.check(L.mace_b200_tc_test_hooks(2_000_000_000, 0), "tc_test_hooks")
+    status.zero_()
+    N.check(L.mace_b200_node_gemm_tc(N.ptr(X), C, xo, 1, N.ptr(Bt), Bt[0].numel(), N.ptr(Y), C, 0, 1, None, n, None,
+                                     0, N.ptr(status), st), "gemm_tc")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    want = X[:, 0].double() @ B[0].double()
+    assert (Y[:, 0].double() - want).abs().max().item() <= 1e-5 * want.abs().max().item()
