@@ -147,3 +147,63 @@ def test_guard_op():
     eat[3] = float("nan")
     with pytest.raises(RuntimeError, match="non-finite or absurd output"):
         ops.guard(eat, 1.0, 100.0, 3)
+
+
+@pytest.mark.parametrize("l1_mode", ["density", "direct"])
+def test_edge_ops_match_c_abi(l1_mode):
+    """The four edge ops, given the engine's tensors, reproduce the C-ABI kernels called with the engine's structs
+    (the op wrappers fill exactly the struct fields the kernels read)."""
+    from mace_onegpu import neighbors as NB
+    from mace_onegpu import structures as S
+
+    mdl = M.default_model(0)
+    pos, Z, box = S.water_box(4, seed=0)
+    cols = torch.as_tensor(S.species_columns(Z, mdl.arch.atomic_numbers))
+    pi, pj, rij = NB.neighbor_list(pos, box, mdl.arch.r_max)
+    n = len(Z)
+    eng = E.ThreePassEngine(mdl, sorted(set(cols.tolist())), chunk=n, device="cuda", l1_mode=l1_mode)
+    plan = eng.plan(pi, pj, rij, cols.cuda(), n, n)
+    eng.evaluate(plan)                                  # fills H1, X2 of the engine's buffers
+    ev, b = eng.eval_struct(plan)
+    L, ops, t = N.lib(), N.ops(), eng.fm.t
+    st = torch.cuda.current_stream().cuda_stream
+    m = N.byref(eng.fm.struct)
+    geo = dict(S=eng.fm.S, M=eng.fm.M, r_lo=eng.fm.r_lo, r_max=eng.fm.r_max, p_cut=float(mdl.arch.num_poly_cutoff))
+    pair = (plan.pi, plan.pj, plan.rij, plan.rowptr, plan.spec)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    # layer 2 forward
+    N.check(L.mace_b200_edge_l2_fwd(m, N.byref(ev), 0, n, st), "edge_l2_fwd")
+    msg0, rho0 = b["s_msg"][:n].clone(), b["s_rho"][:n].clone()
+    msg, rho = torch.zeros_like(b["s_msg"]), torch.zeros_like(b["s_rho"])
+    ops.edge_l2_fwd(t["tab2"], t["tab2_map"], t["wd2"], *pair, b["X2"], msg, rho, status, 0, n, **geo)
+    assert torch.equal(msg[:n], msg0) and torch.equal(rho[:n], rho0)
+    # layer 2 backward (dE/dX2 accumulates with atomics: equal to fp32 summation order)
+    gmsg = torch.randn(b["s_msg"].shape, device="cuda", generator=g)
+    grho = torch.randn(b["s_grho"].shape, device="cuda", generator=g)
+    b["s_msg"].copy_(gmsg)
+    b["s_grho"].copy_(grho)
+    b["PF"].zero_()
+    b["GX2"].zero_()
+    N.check(L.mace_b200_edge_l2_bwd(m, N.byref(ev), 0, n, st), "edge_l2_bwd")
+    PF0, GX0 = b["PF"].clone(), b["GX2"].clone()
+    PF, GX = torch.zeros_like(PF0), torch.zeros_like(GX0)
+    ops.edge_l2_bwd(t["tab2"], t["tab2_map"], t["wd2"], *pair, b["X2"], gmsg, grho, GX, PF, status, 0, n, **geo)
+    assert torch.equal(PF, PF0) and _close(GX, GX0, 1e-6)
+    # layer 1 forward / backward in the engine's form
+    l1d = 1 if eng.fm.l1_density else 0
+    N.check(L.mace_b200_edge_l1_fwd(m, N.byref(ev), 0, n, st), "edge_l1_fwd")
+    msg1 = b["s_msg"].view(-1)[: n * 16 * 128].clone()            # layer-1 rows: [n][16][128] at the front
+    rho1 = b["s_rho"][:n].clone()
+    out, outr = torch.zeros(n * 16 * 128, device="cuda"), torch.zeros(n, device="cuda")
+    ops.edge_l1_fwd(t["tab1"], t["tab1_map"], t["wd1"], l1d, *pair, out, outr, status, 0, n, **geo)
+    assert torch.equal(out, msg1) and torch.equal(outr, rho1)
+    g1 = torch.randn(n * 16 * 128, device="cuda", generator=g)
+    b["s_msg"].view(-1)[: n * 16 * 128].copy_(g1)
+    b["PF"].zero_()
+    N.check(L.mace_b200_edge_l1_bwd(m, N.byref(ev), 0, n, st), "edge_l1_bwd")
+    PF0 = b["PF"].clone()
+    PF = torch.zeros_like(PF0)
+    ops.edge_l1_bwd(t["tab1"], t["tab1_map"], t["wd1"], l1d, *pair, g1, b["s_grho"], PF, status, 0, n, **geo)
+    assert torch.equal(PF, PF0)
+    assert int(status.item()) == 0
