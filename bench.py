@@ -62,7 +62,7 @@ FLOPS_PER_EDGE_L1D = {"edge_l1_fwd": 8 * 64 + 2 * 64 * 16, "edge_l1_bwd": 8 * 64
 TRAFFIC_PER_LAUNCH = {("water_24k", 16384, "edge_l2_bwd"): 560.42e6 + 82.16e6,
                       ("water_1m", 16384, "edge_l2_bwd"): 560.42e6 + 82.16e6}
 EDGE_PASSES = {"edge_l1_fwd": 1, "edge_l1_bwd": 1, "edge_l2_fwd": 1, "edge_l2_bwd": 1}
-ORDER = "morton"      # atom order of the synthetic boxes (--order)
+ORDER = "lammps"      # atom order of the synthetic boxes (--order)
 
 
 def parse():
@@ -83,9 +83,9 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=8, help="water molecules per box edge of the CPU sample")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--skin", type=float, default=2.0, help="ghost shell = r_max + skin (multi-GPU)")
-    ap.add_argument("--order", default="morton", choices=["morton", "grid"],
-                    help="atom order: Morton curve of 3 A cells (spatially sorted, as MD engines pass atoms) or the "
-                         "generator's grid order")
+    ap.add_argument("--order", default="lammps", choices=["lammps", "morton", "grid"],
+                    help="atom order: LAMMPS's spatial sort (bins of 3.5 A, x fastest), a Morton curve of 3 A cells "
+                         "(the reference's standalone driver) or the generator's grid order")
     args = ap.parse_args()
     global ORDER
     ORDER = args.order
@@ -104,8 +104,8 @@ def build_structure(cfg, grid=(1, 1, 1)):
         cell = S.water_box(cfg["n"], seed=cfg["seed"])
     else:
         cell = S.alloy_bcc(cfg["n"], seed=cfg["seed"])
-    if ORDER == "morton":
-        o = S.morton_order(cell[0], cell[2])
+    if ORDER != "grid":
+        o = S.morton_order(cell[0], cell[2]) if ORDER == "morton" else S.lammps_bin_order(cell[0], cell[2])
         cell = (cell[0][o], cell[1][o], cell[2])
     return cell if tuple(grid) == (1, 1, 1) else S.tile(*cell, grid)
 

@@ -260,7 +260,44 @@ __global__ void k_csr_rows(const int32_t* __restrict__ pi, int64_t e0, int64_t e
   }
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_status(status, MB_ST_UNSORTED);
 }
+// Smallest and largest sender of a chunk's edges: out = (min, max) of pair_j[e0, e1), combined with atomics into
+// the (INT32_MAX, -1) that k_range_init wrote (an empty range leaves those).
+__global__ void k_range_init(int32_t* out) {
+  out[0] = INT32_MAX;
+  out[1] = -1;
+}
+
+__global__ void k_sender_range(const int32_t* __restrict__ pj, int64_t e0, int64_t e1, int32_t* out) {
+  int lo = INT32_MAX, hi = -1;
+  for (int64_t e = e0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < e1; e += (int64_t)gridDim.x * blockDim.x) {
+    const int j = __ldg(pj + e);
+    lo = min(lo, j);
+    hi = max(hi, j);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if ((threadIdx.x & 31) == 0 && hi >= 0) {
+    atomicMin(out, lo);
+    atomicMax(out + 1, hi);
+  }
+}
 }  // namespace mb
+
+extern "C" int mace_b200_sender_range(const int32_t* pair_j, int64_t e0, int64_t e1, int32_t* out, void* stream) {
+  if (!pair_j || !out || e0 < 0 || e1 < e0) {
+    set_error("sender_range: bad arguments (edges [%lld, %lld))", (long long)e0, (long long)e1);
+    return MB_E_ARG;
+  }
+  k_range_init<<<1, 1, 0, (cudaStream_t)stream>>>(out);
+  if (int rc = check_launch("sender_range")) return rc;
+  if (e1 == e0) return 0;
+  const int64_t blocks = (e1 - e0 + 1023) / 1024 < 296 ? (e1 - e0 + 1023) / 1024 : 296;
+  k_sender_range<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(pair_j, e0, e1, out);
+  return check_launch("sender_range");
+}
 
 extern "C" int mace_b200_csr_rows(const int32_t* pair_i, int64_t e0, int64_t e1, int32_t a, int32_t b,
                                   int32_t* rowptr, uint32_t* status, void* stream) {

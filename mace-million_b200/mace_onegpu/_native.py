@@ -89,6 +89,7 @@ _SIGS = {
     "mace_b200_verlet_filter": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_f64, c_vp, c_vp, c_vp, c_vp, c_vp,
                                         c_vp, c_vp]),
     "mace_b200_csr_rows": (c_i32, [c_vp, c_i64, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "mace_b200_sender_range": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp]),
     "mace_b200_tc_test_hooks": (c_i32, [c_u64, c_i32]),
 }
 

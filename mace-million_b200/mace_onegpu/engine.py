@@ -14,6 +14,7 @@ Folding (exact algebra, fp64 on the host, then fp32 on the device):
 """
 from __future__ import annotations
 
+import heapq
 import math
 import os
 
@@ -373,6 +374,11 @@ class ThreePassEngine:
         env = os.environ.get("MACE_B200_X1_CACHE")
         self.x1_cache = x1_cache if x1_cache is not None else (None if env is None else env != "0")
         self.graphs = os.environ.get("MACE_B200_GRAPHS", "0") == "1"
+        # streamed single-GPU pair lists: run every pass-B chunk as soon as pass A has covered its senders
+        self.pipeline = os.environ.get("MACE_B200_PIPELINE", "1") != "0"
+        self._dep_host = None
+        self.last_schedule = None         # "serial", "overlap", "pipelined" or "graph": how the last call ran
+        self.early_b_chunks = 0           # pipelined: pass-B chunks issued before pass A's last chunk
         self._graph = None
         self.captures = 0
         self.fm = FoldedModel(model, cols, spline_grid=spline_grid, device=self.device, use_tc=use_tc, l1_mode=l1_mode)
@@ -533,6 +539,71 @@ class ThreePassEngine:
         N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
         return PFd, fbits
 
+    _LOOKAHEAD = 2      # pipelined schedule: pass A chunk k is issued once chunk k - 2's sender range is known
+
+    def _run_pipelined(self, plan, ev, b, dep_host, ready):
+        """Single-GPU evaluation of a streamed pair list (no ghosts) with pass B interleaved into pass A.  Pass-B chunk
+        c reads the X2 rows of its senders only, so it can run once pass A (and the X2 GEMM) has covered the chunks
+        up to need(c) = max(c, largest sender of c // chunk); the side stream reports each chunk's sender range
+        (mace_b200_sender_range) together with its arrival, and the host issues, after pass-A chunk k, every known
+        chunk with need(c) <= k.  With spatially sorted atoms (LAMMPS sorts them into bins), need(c) is c + 2 or
+        c + 3 for almost every chunk, so the pair list's host-to-device transfer hides under pass B instead of
+        under pass A alone.  Pass C follows all of pass B as in _run.  Timing marks: t_A covers pass A with the
+        pass-B chunks interleaved in it, t_B the remaining pass-B chunks and the G1 fold."""
+        L = N.lib()
+        m = N.byref(self.fm.struct)
+        evp = N.byref(ev)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        nl, nch, C_ = plan.nl, plan.n_chunks, self.chunk
+        b["eat"].zero_()
+        b["PF"].zero_()
+        PFd = self._get("PFd", (plan.P, 3), torch.float64)
+        fbits = self._get("fmax", (1,), torch.int32)
+        fbits.zero_()
+        if ev.done_ev:
+            ev.pf_out, ev.fmax_bits = N.ptr(PFd), N.ptr(fbits)
+        marks = self._pass_marks() if self.pass_timing else None
+        self._marks_valid = marks is not None
+        mark = (lambda k: marks[k].record()) if marks else (lambda k: None)
+        pend = []                 # heap of (need, chunk) for chunks whose sender range is known
+        known = 0
+
+        def learn(upto):
+            nonlocal known
+            while known < upto:
+                ready[known].synchronize()
+                hi = int(dep_host[known, 1])
+                need = known if hi < 0 else min(max(known, hi // C_), nch - 1)
+                heapq.heappush(pend, (need, known))
+                known += 1
+
+        def run_b(c):
+            N.check(L.mace_b200_pass_b_chunks(m, evp, c, c + 1, st), "pass_b")
+
+        mark(0)
+        early = 0
+        for k in range(nch):
+            N.check(L.mace_b200_pass_a_chunks(m, evp, k, k + 1, st), "pass_a")
+            N.check(L.mace_b200_x2_rows(m, evp, k * C_, min((k + 1) * C_, nl), st), "x2_rows")
+            learn(max(0, k + 1 - self._LOOKAHEAD))
+            while pend and pend[0][0] <= k:
+                run_b(heapq.heappop(pend)[1])
+                early += k < nch - 1
+        self.early_b_chunks = early
+        mark(1)
+        mark(2)
+        learn(nch)
+        while pend:
+            run_b(heapq.heappop(pend)[1])
+        N.check(L.mace_b200_fold_g1(m, evp, 0, plan.nt, st), "fold_g1")
+        mark(3)
+        mark(4)
+        N.check(L.mace_b200_pass_c(m, evp, st), "pass_c")
+        mark(5)
+        N.check(L.mace_b200_finalize(m, evp, N.ptr(plan.perm), N.ptr(PFd), N.ptr(fbits), st), "finalize")
+        mark(6)
+        return PFd, fbits
+
     _PASSES = ("A", "xchg_fwd", "B", "xchg_rev", "C", "finalize")
 
     def _pass_marks(self):
@@ -585,6 +656,7 @@ class ThreePassEngine:
         deferred = plan.host_src is not None
         use_graph = self.graphs if graph is None else graph
         if use_graph and forward_exchange is None and reverse_exchange is None and not deferred:
+            self.last_schedule = "graph"
             b, PFd, fbits = self._evaluate_graph(plan)
         else:
             ev, b = self.eval_struct(plan)
@@ -594,13 +666,20 @@ class ThreePassEngine:
             b["status"].zero_()                           # before the side stream's CSR checks can set bits
             if deferred or host_pf is not None:
                 if self._io is None:
-                    self._io = torch.cuda.Stream(self.device)
+                    # high priority: its small CSR / sender-range kernels must not queue behind the pass kernels
+                    self._io = torch.cuda.Stream(self.device, priority=-1)
                 io = self._io
                 io.wait_stream(cur)
+            pipe = deferred and self.pipeline and halo is None and plan.nt == plan.nl and nch > 1
             if deferred:
                 ops = N.ops()
                 h_pi, h_pj, h_rij = plan.host_src
                 waits = self._events("wait", nch)
+                if pipe:
+                    dep_dev = self._get("sender_range", (nch, 2), torch.int32)
+                    if self._dep_host is None or self._dep_host.shape[0] < nch:
+                        self._dep_host = torch.empty(nch, 2, dtype=torch.int32, pin_memory=True)
+                    dep_host = self._dep_host
                 with torch.cuda.stream(io):
                     if self.pass_timing:
                         self._h2d_marks = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -612,10 +691,14 @@ class ThreePassEngine:
                         plan.rij[e0:e1].copy_(h_rij[e0:e1], non_blocking=True)
                         ops.csr_rows(plan.pi, e0, e1, int(plan.bounds[k]), int(plan.bounds[k + 1]), plan.rowptr,
                                      b["status"])
+                        if pipe:
+                            N.check(N.lib().mace_b200_sender_range(N.ptr(plan.pj), e0, e1, N.ptr(dep_dev[k]),
+                                                                   io.cuda_stream), "sender_range")
+                            dep_host[k].copy_(dep_dev[k], non_blocking=True)
                         waits[k].record(io)
                     if self.pass_timing:
                         self._h2d_marks[1].record(io)
-                for t in (plan.pi, plan.pj, plan.rij, plan.rowptr, b["status"]):
+                for t in (plan.pi, plan.pj, plan.rij, plan.rowptr, b["status"]) + ((dep_dev,) if pipe else ()):
                     t.record_stream(io)
                 arr = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in waits])
                 keep.append(arr)
@@ -626,8 +709,12 @@ class ThreePassEngine:
                 arr2 = (N.ctypes.c_void_p * nch)(*[e.cuda_event for e in done])
                 keep.append(arr2)
                 ev.done_ev = N.ctypes.addressof(arr2)
-            if halo is not None and plan.nt > plan.nl:
+            self.last_schedule = "overlap" if halo is not None and plan.nt > plan.nl else \
+                "pipelined" if pipe else "serial"
+            if self.last_schedule == "overlap":
                 PFd, fbits = self._run_overlap(plan, ev, b, halo)
+            elif pipe:
+                PFd, fbits = self._run_pipelined(plan, ev, b, dep_host, waits)
             else:
                 PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange, zero_status=False)
             if out_host:

@@ -90,6 +90,17 @@ def morton_order(pos, box, cell: float = 3.0) -> np.ndarray:
     return np.argsort(code, kind="stable")
 
 
+def lammps_bin_order(pos, box, binsize: float = 3.5) -> np.ndarray:
+    """Permutation into the order of LAMMPS's spatial atom sort (atom_modify sort, on by default every 1000 steps):
+    cubic-ish bins of about `binsize` A (LAMMPS's default is half the neighbour cutoff, (5 + 2) / 2 A for a 5 A
+    model with a 2 A skin), numbered x fastest, then y, then z; atoms of one bin keep their relative order.  A
+    chunk of consecutive receivers is then a slab a few bins thick, whose senders lie in the neighbouring slabs."""
+    pos = np.remainder(np.asarray(pos, dtype=np.float64), box)
+    nb = np.maximum(np.floor(np.asarray(box) / binsize).astype(np.int64), 1)
+    c = np.minimum((pos / (np.asarray(box) / nb)).astype(np.int64), nb - 1)
+    return np.argsort((c[:, 2] * nb[1] + c[:, 1]) * nb[0] + c[:, 0], kind="stable")
+
+
 def species_columns(Z, atomic_numbers) -> np.ndarray:
     """Model one-hot column of every atom (index into atomic_numbers)."""
     lut = {int(z): i for i, z in enumerate(atomic_numbers)}

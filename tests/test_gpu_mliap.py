@@ -2,7 +2,8 @@
 
 Device-resident inputs against the CPU fp64 oracle (the north_star tolerances); pinned host inputs and outputs (the
 engine streams senders / vectors in chunk by chunk during pass A and hands every finished chunk's pair forces to
-the host during pass C) against the device-resident call; shuffled host input (no overlap: the engine sorts);
+the host during pass C) against the device-resident call; the pipelined pass A / B schedule of a streamed pair list
+against the serial one; shuffled host input (no overlap: the engine sorts);
 a pickle round trip of the plugin object (LAMMPS unpickles it from the model file)."""
 import dataclasses
 import io
@@ -74,6 +75,38 @@ def test_pinned_host_io_overlap_matches_device(setup):
     mli.compute_forces(host)
     torch.cuda.synchronize()
     assert (host.pair_forces - setup["pf"]).abs().max() < F_TOL
+
+
+def test_pipelined_schedule_matches_serial():
+    """A streamed pair list of a box long in z, in LAMMPS's bin order (z slabs; 24 chunks of 32 receivers): pass-B
+    chunks run interleaved with pass A as soon as their senders are covered.  Same energies and pair forces as the
+    serial schedule; a Morton-ordered copy (wider sender ranges) has more chunks wait for late pass-A chunks."""
+    mdl = M.default_model(0)
+    pos, Z, box = S.water_box(4, 4, 16, seed=3)
+    for order in ("lammps", "morton"):
+        o = S.lammps_bin_order(pos, box) if order == "lammps" else S.morton_order(pos, box)
+        p, z = pos[o], Z[o]
+        cols = torch.as_tensor(S.species_columns(z, mdl.arch.atomic_numbers))
+        pi, pj, rij = NB.neighbor_list(p, box, mdl.arch.r_max)
+        s = dict(pi=pi, pj=pj, rij=rij, cols=cols, n=len(z))
+        mli = ThreePassMLIAP(mdl, chunk=32)
+        pip = _host_data(s)
+        mli.compute_forces(pip)                          # the engine's default schedule for this input
+        assert mli._eng.last_schedule == "pipelined"
+        if order == "lammps":
+            assert mli._eng.early_b_chunks >= 12          # most chunks ran before pass A's last chunk
+        mli._eng.pipeline = False
+        ser = _host_data(s)
+        mli.compute_forces(ser)
+        assert mli._eng.last_schedule == "serial"
+        torch.cuda.synchronize()
+        for _ in range(2):
+            assert (pip.eatoms - ser.eatoms).abs().max() < 1e-9
+            assert (pip.pair_forces - ser.pair_forces).abs().max() < 1e-5 * ser.pair_forces.abs().max() + 1e-7
+            mli._eng.pipeline = True                      # again, with the side stream and events reused
+            mli.compute_forces(pip)
+            assert mli._eng.last_schedule == "pipelined"
+            torch.cuda.synchronize()
 
 
 def test_shuffled_host_inputs(setup):

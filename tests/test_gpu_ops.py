@@ -5,7 +5,8 @@
   fp64 oracle's channelwise convolution (oracle/mace_ref.py MaceRef.conv, differentiated by torch autograd), for the
   layer-1 and layer-2 path tables, with edges in random order (the op groups them by receiver and by sender).
 * build_tables against the C-ABI table builder; symcon_fwd / _bwd against direct C-ABI calls; node_gemm against
-  torch; pack_halo / unpack_halo_add / csr_rows against torch indexing; the output guard's RuntimeError."""
+  torch; pack_halo / unpack_halo_add / csr_rows against torch indexing; the C-ABI sender_range against torch min / max;
+  the output guard's RuntimeError."""
 import dataclasses
 
 import pytest
@@ -136,6 +137,22 @@ def test_halo_pack_unpack_and_csr_rows_ops():
     assert int(status.item()) == 0
     ops.csr_rows(pi.flip(0).contiguous(), 0, 1000, 0, 50, rowptr, status)     # not sorted: flagged
     assert int(status.item()) == 64
+
+
+def test_sender_range():
+    """mace_b200_sender_range: (min, max) of pair_j over an edge range, (INT32_MAX, -1) for an empty range."""
+    L = N.lib()
+    g = torch.Generator(device="cuda").manual_seed(8)
+    pj = torch.randint(0, 1_000_000, (3_000_000,), device="cuda", dtype=torch.int32, generator=g)
+    out = torch.zeros(4, 2, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    cases = [(0, 3_000_000), (5, 6), (1_234_567, 2_500_001), (10, 10)]
+    for q, (e0, e1) in enumerate(cases):
+        N.check(L.mace_b200_sender_range(N.ptr(pj), e0, e1, N.ptr(out[q]), st), "sender_range")
+    torch.cuda.synchronize()
+    for q, (e0, e1) in enumerate(cases[:3]):
+        assert out[q].tolist() == [int(pj[e0:e1].min()), int(pj[e0:e1].max())]
+    assert out[3].tolist() == [2**31 - 1, -1]
 
 
 def test_guard_op():
