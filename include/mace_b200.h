@@ -330,9 +330,10 @@ int mace_b200_csr_rows(const int32_t* pair_i, int64_t e0, int64_t e1, int32_t a,
                        uint32_t* status, void* stream);
 
 /* Smallest and largest sender of a chunk of a streamed pair list: out[0] = min, out[1] = max of pair_j[e0, e1)
- * ((INT32_MAX, -1) for an empty range), written on the stream.  No counterpart in the reference, which copies the
- * whole pair list before it starts pass A: the engine reads the range back per chunk to run every pass-B chunk as
- * soon as pass A has produced the features of all its senders, while later chunks are still arriving. */
+ * ((INT32_MAX, -1) for an empty range), written on the stream.  No counterpart in the reference, whose pair list is
+ * already in device memory: the engine reads the range back per chunk of a list streamed from host memory, to run
+ * every pass-B chunk as soon as pass A has produced the features of all its senders while later chunks still
+ * arrive. */
 int mace_b200_sender_range(const int32_t* pair_j, int64_t e0, int64_t e1, int32_t* out, void* stream);
 
 #ifdef __cplusplus

@@ -541,15 +541,17 @@ class ThreePassEngine:
 
     _LOOKAHEAD = 2      # pipelined schedule: pass A chunk k is issued once chunk k - 2's sender range is known
 
-    def _run_pipelined(self, plan, ev, b, dep_host, ready):
-        """Single-GPU evaluation of a streamed pair list (no ghosts) with pass B interleaved into pass A.  Pass-B chunk
-        c reads the X2 rows of its senders only, so it can run once pass A (and the X2 GEMM) has covered the chunks
-        up to need(c) = max(c, largest sender of c // chunk); the side stream reports each chunk's sender range
+    def _run_pipelined(self, plan, ev, b, dep_host, ready, forward_exchange=None, reverse_exchange=None):
+        """Evaluation of a streamed pair list with pass B interleaved into pass A.  Pass-B chunk c reads the X2 rows
+        of its senders only, so it can run once pass A (and the X2 GEMM) has covered the chunks up to
+        need(c) = max(c, largest sender of c // chunk); the side stream reports each chunk's sender range
         (mace_b200_sender_range) together with its arrival, and the host issues, after pass-A chunk k, every known
-        chunk with need(c) <= k.  With spatially sorted atoms (LAMMPS sorts them into bins), need(c) is c + 2 or
-        c + 3 for almost every chunk, so the pair list's host-to-device transfer hides under pass B instead of
-        under pass A alone.  Pass C follows all of pass B as in _run.  Timing marks: t_A covers pass A with the
-        pass-B chunks interleaved in it, t_B the remaining pass-B chunks and the G1 fold."""
+        chunk with need(c) <= k.  A chunk with a ghost sender (index >= nlocal) waits for the H1 forward exchange,
+        which follows the last pass-A chunk as in _run.  With spatially sorted atoms (LAMMPS sorts them into bins;
+        a domain ordered interior first, domain.Decomposition), need(c) is c + 2 or c + 3 for almost every chunk
+        without ghost senders, so the pair list's host-to-device transfer hides under pass B instead of under pass
+        A alone.  Pass C follows all of pass B.  Timing marks: t_A covers pass A with the pass-B chunks interleaved
+        in it, t_B the remaining pass-B chunks and the G1 fold."""
         L = N.lib()
         m = N.byref(self.fm.struct)
         evp = N.byref(ev)
@@ -573,7 +575,7 @@ class ThreePassEngine:
             while known < upto:
                 ready[known].synchronize()
                 hi = int(dep_host[known, 1])
-                need = known if hi < 0 else min(max(known, hi // C_), nch - 1)
+                need = known if hi < 0 else nch if hi >= nl else max(known, hi // C_)
                 heapq.heappush(pend, (need, known))
                 known += 1
 
@@ -591,12 +593,18 @@ class ThreePassEngine:
                 early += k < nch - 1
         self.early_b_chunks = early
         mark(1)
+        if plan.nt > nl:
+            if forward_exchange is not None:
+                forward_exchange(b["H1"].view(plan.nt, 4 * C))
+            N.check(L.mace_b200_x2_rows(m, evp, nl, plan.nt, st), "x2_rows")
         mark(2)
         learn(nch)
         while pend:
             run_b(heapq.heappop(pend)[1])
         N.check(L.mace_b200_fold_g1(m, evp, 0, plan.nt, st), "fold_g1")
         mark(3)
+        if reverse_exchange is not None and plan.nt > nl:
+            reverse_exchange(b["G1"].view(plan.nt, 4 * C))
         mark(4)
         N.check(L.mace_b200_pass_c(m, evp, st), "pass_c")
         mark(5)
@@ -670,7 +678,7 @@ class ThreePassEngine:
                     self._io = torch.cuda.Stream(self.device, priority=-1)
                 io = self._io
                 io.wait_stream(cur)
-            pipe = deferred and self.pipeline and halo is None and plan.nt == plan.nl and nch > 1
+            pipe = deferred and self.pipeline and not (halo is not None and plan.nt > plan.nl) and nch > 1
             if deferred:
                 ops = N.ops()
                 h_pi, h_pj, h_rij = plan.host_src
@@ -714,7 +722,7 @@ class ThreePassEngine:
             if self.last_schedule == "overlap":
                 PFd, fbits = self._run_overlap(plan, ev, b, halo)
             elif pipe:
-                PFd, fbits = self._run_pipelined(plan, ev, b, dep_host, waits)
+                PFd, fbits = self._run_pipelined(plan, ev, b, dep_host, waits, forward_exchange, reverse_exchange)
             else:
                 PFd, fbits = self._run(plan, ev, b, forward_exchange, reverse_exchange, zero_status=False)
             if out_host:

@@ -3,7 +3,7 @@
 Device-resident inputs against the CPU fp64 oracle (the north_star tolerances); pinned host inputs and outputs (the
 engine streams senders / vectors in chunk by chunk during pass A and hands every finished chunk's pair forces to
 the host during pass C) against the device-resident call; the pipelined pass A / B schedule of a streamed pair list
-against the serial one; shuffled host input (no overlap: the engine sorts);
+against the serial one, without and with ghost atoms; shuffled host input (no overlap: the engine sorts);
 a pickle round trip of the plugin object (LAMMPS unpickles it from the model file)."""
 import dataclasses
 import io
@@ -107,6 +107,46 @@ def test_pipelined_schedule_matches_serial():
             mli.compute_forces(pip)
             assert mli._eng.last_schedule == "pipelined"
             torch.cuda.synchronize()
+
+
+def test_pipelined_schedule_with_ghosts():
+    """Streamed pair list with explicit ghost atoms (the periodic images across the z faces of a box long in z, in
+    LAMMPS's bin order) and owner-map exchanges: the chunks in the middle of the box have no ghost sender and run
+    during pass A, the end chunks after the H1 exchange.  Same results as the serial schedule and as the same box
+    without ghosts (minimum image)."""
+    mdl = M.default_model(0)
+    pos, Z, box = S.water_box(4, 4, 16, seed=4)
+    o = S.lammps_bin_order(pos, box)
+    pos, Z = pos[o], Z[o]
+    n = len(Z)
+    cols = torch.as_tensor(S.species_columns(Z, mdl.arch.atomic_numbers))
+    pi, pj, rij = NB.neighbor_list(pos, box, mdl.arch.r_max)
+    d = torch.as_tensor(pos)[pi.long()] - torch.as_tensor(pos)[pj.long()]
+    cross = (rij[:, 2] - d[:, 2]).abs() > 1e-9                 # pairs across a z face: the sender is a ghost
+    pj2 = pj.clone()
+    pj2[cross] = n + torch.arange(int(cross.sum()), dtype=pj.dtype)
+    owner = torch.cat([torch.arange(n), pj[cross].long()])
+    cols2 = torch.cat([cols, cols[pj[cross].long()]])
+
+    def ghost_data():
+        return MLIAPData(pi.contiguous().pin_memory(), pj2.contiguous().pin_memory(), rij.contiguous().pin_memory(),
+                         cols2.clone().pin_memory(), n, owner=owner, host_outputs=True)
+
+    mli = ThreePassMLIAP(mdl, chunk=32)
+    pip = ghost_data()
+    mli.compute_forces(pip)
+    assert mli._eng.last_schedule == "pipelined"
+    assert mli._eng.early_b_chunks >= 8
+    mli._eng.pipeline = False
+    ser = ghost_data()
+    mli.compute_forces(ser)
+    assert mli._eng.last_schedule == "serial"
+    plain = _host_data(dict(pi=pi, pj=pj, rij=rij, cols=cols, n=n))
+    mli.compute_forces(plain)
+    torch.cuda.synchronize()
+    for other in (ser, plain):
+        assert (pip.eatoms - other.eatoms).abs().max() < 1e-9
+        assert (pip.pair_forces - other.pair_forces).abs().max() < 1e-5 * other.pair_forces.abs().max() + 1e-7
 
 
 def test_shuffled_host_inputs(setup):
