@@ -9,11 +9,15 @@
 // problems of the group:
 //   warps 0-3  producers: thread p owns row p of the tile.  Its 128-byte slice of each K block is prefetched
 //              TC_RAW blocks ahead with cp.async into a padded raw ring (no registers held), then split into
-//              tf32 hi / lo and stored into the swizzled operand stage; thread 0 also fetches the stage's B hi / lo
-//              blocks with two 16 KB cp.async.bulk copies (no multicast).
-//   warp 8     barrier init, TMEM allocation (two 128-column accumulators) and, on lane 0, the MMA issue:
-//              12 tcgen05.mma kind::tf32 (M = N = 128, K = 8) per K block, tcgen05.commit -> stage-empty barrier,
-//              and after a tile's last block -> accumulator-full barrier.
+//              tf32 hi / lo and written with tcgen05.st into the stage's A columns of TMEM (row p = TMEM lane p);
+//              thread 0 also fetches the stage's B hi / lo blocks into shared memory with two 16 KB
+//              cp.async.bulk copies (no multicast).
+//   warp 8     barrier init, TMEM allocation (two 128-column accumulators + 64 A columns per stage) and, on
+//              lane 0, the MMA issue: 12 tcgen05.mma kind::tf32 (M = N = 128, K = 8, A from TMEM, B from shared
+//              memory) per K block, tcgen05.commit -> stage-empty barrier, and after a tile's last block ->
+//              accumulator-full barrier.  With A in TMEM the MMAs read half the shared-memory bytes (49.5 against
+//              54.4 ms of node GEMMs per 1.03M-atom evaluation with A staged in shared memory, MB_TC_A_TMEM = 0);
+//              deeper stage / raw rings (3 or 4 stages, 6 raw blocks) measured the same.
 //   warps 4-7  epilogue: tcgen05.ld 32x32b of the finished accumulator (warp w reads TMEM lanes 32 (w % 4) ..,
 //              one row per lane), row scale 1 / (rho + 1), then a transpose through shared memory so that the
 //              optional accumulate load and the store of every 32-column chunk go out as full 128-byte row
@@ -27,20 +31,39 @@ namespace mb {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32;
 constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 4;          // 16 KB: one operand plane of one K block
-constexpr int TC_STAGES = 2;                               // operand stages (A hi, A lo, B hi, B lo)
-constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;
-constexpr int TC_RAW = 4;                                  // cp.async depth of the raw A ring, in K blocks
+#ifndef MB_TC_STAGES
+#define MB_TC_STAGES 2
+#endif
+#ifndef MB_TC_RAW
+#define MB_TC_RAW 4
+#endif
+constexpr int TC_STAGES = MB_TC_STAGES;                    // operand stages
+// A hi / lo of a stage: in TMEM (MB_TC_A_TMEM = 1; the MMA reads A from TMEM and only B from shared memory) or in
+// shared memory beside B (0)
+#ifndef MB_TC_A_TMEM
+#define MB_TC_A_TMEM 1
+#endif
+#if MB_TC_A_TMEM
+constexpr int TC_STAGE_BYTES = 2 * TC_TILE_BYTES;          // B hi, B lo
+constexpr int TC_TMEM_COLS = 512;                          // two accumulators + A hi / lo (2 x 32 columns) per stage
+#else
+constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;          // A hi, A lo, B hi, B lo
+constexpr int TC_TMEM_COLS = 2 * TC_BN;
+#endif
+constexpr int TC_A_COL = 2 * TC_BN;                        // first TMEM column of the A stages
+constexpr int TC_RAW = MB_TC_RAW;                          // cp.async depth of the raw A ring, in K blocks
 constexpr int TC_RAW_ROW = 144;                            // one row's 128-byte K slice + 16 bytes of bank padding
 constexpr int TC_RAW_BYTES = TC_BM * TC_RAW_ROW;
 constexpr int TC_EPI_ROW = 33;                             // epilogue transpose: 32 floats per row + 1 (bank spread)
 constexpr int TC_EPI_BYTES = 4 * 32 * TC_EPI_ROW * 4;      // one 32-row x 32-column chunk per epilogue warp
 constexpr int TC_THREADS = 288;                            // 4 producer warps, 4 epilogue warps, 1 MMA warp
 constexpr int TC_MMA_WARP = 8;
-constexpr int TC_ACC_COLS = 2 * TC_BN;
+static_assert(!MB_TC_A_TMEM || TC_A_COL + TC_STAGES * 2 * TC_BK <= TC_TMEM_COLS, "TMEM columns");
 constexpr int TC_RAW_OFF = TC_STAGES * TC_STAGE_BYTES;
 constexpr int TC_EPI_OFF = TC_RAW_OFF + TC_RAW * TC_RAW_BYTES;
 constexpr int TC_BAR_OFF = TC_EPI_OFF + TC_EPI_BYTES;
 constexpr int TC_SMEM = TC_BAR_OFF + 256 + 1024;           // + barriers / TMEM slot / flag + alignment slack
+static_assert(TC_SMEM <= 227 * 1024, "shared memory per CTA");
 // Every mbarrier wait gives up after g_tc_wait_ns nanoseconds of %globaltimer (default 2 s; a GEMM tile takes
 // microseconds).  mace_b200_tc_test_hooks shortens it and can make one producer arrival go missing, so that a test
 // drives the timeout path (MB_ST_TC_TIMEOUT, drain, TMEM release) without any fault.
@@ -93,6 +116,28 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// the same with A read from TMEM (tmem_a: lane 0 and the first of the 8 columns of this K step, one row per lane)
+__device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// 32 consecutive TMEM columns of this warp's 32 lanes from 32 registers per thread (warp-collective)
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -198,7 +243,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
 
   if (warp == TC_MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem)),
-                 "r"(TC_ACC_COLS)
+                 "r"(TC_TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     if (lane == 0) {
@@ -252,7 +297,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     for (int q = 0; q < TC_RAW; ++q) issue_next(q);
     int seq = 0;                                   // K blocks consumed (stage / phase counter)
     TcRow rw = tc_row(grp, blockIdx.x, p);
-    for (int tile = blockIdx.x; tile < n_tiles && !*failed; tile += gridDim.x) {
+    // every exit decision is warp-uniform: the loop body holds warp-collective tcgen05.st.sync.aligned
+    for (int tile = blockIdx.x; tile < n_tiles && !__shfl_sync(0xffffffffu, *failed, 0); tile += gridDim.x) {
       const GemmProblem& g = grp.p[rw.pi];
       const int nk = rw.nk;
       const bool have = rw.a != nullptr;
@@ -265,8 +311,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         for (int q = 0; q < 8; ++q)
           v[q] = have ? *reinterpret_cast<const float4*>(src + 16 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
         issue_next(slot);                          // the slot has been read: refill it TC_RAW blocks ahead
+#if MB_TC_A_TMEM
+        uint32_t ahi[32], alo[32];                 // split before the wait, so that the wait covers it
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float c4[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float h = tf32_rna(c4[j]);
+            ahi[4 * q + j] = __float_as_uint(h);
+            alo[4 * q + j] = __float_as_uint(tf32_rna(c4[j] - h));
+          }
+        }
+#endif
         // stage s free once the MMAs of its previous use completed (first use: the preceding phase counts done)
-        if (!mbar_wait(&B.empty[s], ((seq / TC_STAGES) & 1) ^ 1)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&B.empty[s], ((seq / TC_STAGES) & 1) ^ 1))) {
           *failed = 1;
           break;
         }
@@ -275,9 +334,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
           const int seg = (kb * TC_BK) / MB_C, kin = kb * TC_BK - seg * MB_C;
           const float* bsrc = g.B + (int64_t)seg * MB_C * MB_C + (int64_t)(kin / TC_BK) * (TC_BM * TC_BK);
           mbar_arrive_tx(&B.bfull[s], 2 * TC_TILE_BYTES);
-          bulk_g2s(st + 2 * TC_TILE_BYTES, bsrc, TC_TILE_BYTES, &B.bfull[s]);
-          bulk_g2s(st + 3 * TC_TILE_BYTES, bsrc + g.plane, TC_TILE_BYTES, &B.bfull[s]);
+          bulk_g2s(st + TC_STAGE_BYTES - 2 * TC_TILE_BYTES, bsrc, TC_TILE_BYTES, &B.bfull[s]);
+          bulk_g2s(st + TC_STAGE_BYTES - TC_TILE_BYTES, bsrc + g.plane, TC_TILE_BYTES, &B.bfull[s]);
         }
+#if MB_TC_A_TMEM
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(TC_A_COL + s * 2 * TC_BK);
+        tmem_st32(ta, ahi);
+        tmem_st32(ta + TC_BK, alo);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+#else
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float4 hi, lo;
@@ -290,6 +357,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
           *reinterpret_cast<float4*>(st + TC_TILE_BYTES + off) = lo;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+#endif
         // test hook (off unless mace_b200_tc_test_hooks armed it): one arrival of CTA 0's first K block goes missing
         const bool skip = seq == 0 && p == 0 && blockIdx.x == 0 && *(volatile int*)&g_tc_skip_arrival &&
                           atomicExch(&g_tc_skip_arrival, 0);
@@ -381,9 +449,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_hi = smem_u32(smem + s * TC_STAGE_BYTES), a_lo = a_hi + TC_TILE_BYTES;
-        const uint32_t b_hi = a_hi + 2 * TC_TILE_BYTES, b_lo = a_hi + 3 * TC_TILE_BYTES;
         const uint32_t d = tmem + (uint32_t)(a * TC_BN);
+        const uint32_t b_hi = smem_u32(smem + (s + 1) * TC_STAGE_BYTES - 2 * TC_TILE_BYTES), b_lo = b_hi + TC_TILE_BYTES;
+#if MB_TC_A_TMEM
+        const uint32_t a_hi = tmem + (uint32_t)(TC_A_COL + s * 2 * TC_BK), a_lo = a_hi + TC_BK;
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 8; ++kk) {
+          const uint32_t ko = kk * 32;               // 8 tf32 = 32 bytes along K inside B's swizzle atom
+          mma_tf32_ts(d, a_hi + 8 * kk, sw128_desc(b_hi + ko), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(d, a_hi + 8 * kk, sw128_desc(b_lo + ko), idesc, 1u);
+          mma_tf32_ts(d, a_lo + 8 * kk, sw128_desc(b_hi + ko), idesc, 1u);
+        }
+#else
+        const uint32_t a_hi = smem_u32(smem + s * TC_STAGE_BYTES), a_lo = a_hi + TC_TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 8; ++kk) {
           const uint32_t ko = kk * 32;               // 8 tf32 = 32 bytes along K inside the swizzle atom
@@ -391,6 +469,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
           mma_tf32(d, sw128_desc(a_hi + ko), sw128_desc(b_lo + ko), idesc, 1u);
           mma_tf32(d, sw128_desc(a_lo + ko), sw128_desc(b_hi + ko), idesc, 1u);
         }
+#endif
         mma_commit(&B.empty[s]);
         last_bar = &B.empty[s];
         last_par = ph;
@@ -406,13 +485,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     // after a timeout: wait (bounded) for the MMAs already issued before the TMEM is freed
     if (*failed && last_bar) mbar_wait(last_bar, last_par);
   }
-  if (tid == 0 && *failed) set_status(grp.status, MB_ST_TC_TIMEOUT);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  // after every role has stopped: a producer that never had to wait may finish before the MMA thread gives up
+  if (tid == 0 && *failed) set_status(grp.status, MB_ST_TC_TIMEOUT);
   if (warp == TC_MMA_WARP) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_ACC_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
   }
 }
 
