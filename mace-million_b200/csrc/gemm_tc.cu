@@ -5,23 +5,27 @@
 // split on the fly: a_hi = rna_tf32(a), a_lo = rna_tf32(a - a_hi), and D = a_hi b_hi + a_hi b_lo + a_lo b_hi
 // accumulates in fp32 in TMEM (the lo*lo term, ~2^-22 relative, is dropped).
 //
-// Persistent, warp-specialised CTA (one per SM, 288 threads), static round-robin over the 128-row tiles of all
-// problems of the group:
-//   warps 0-3  producers: thread p owns row p of the tile.  Its 128-byte slice of each K block is prefetched
-//              TC_RAW blocks ahead with cp.async into a padded raw ring (no registers held), then split into
-//              tf32 hi / lo and written with tcgen05.st into the stage's A columns of TMEM (row p = TMEM lane p);
-//              thread 0 also fetches the stage's B hi / lo blocks into shared memory with two 16 KB
-//              cp.async.bulk copies (no multicast).
-//   warp 8     barrier init, TMEM allocation (two 128-column accumulators + 64 A columns per stage) and, on
+// Persistent, warp-specialised CTA (one per SM; TC_PG = 2, TC_EPW = 8: 544 threads), static round-robin over the
+// 128-row tiles of all problems of the group:
+//   producers  TC_PG groups of 4 warps; group g makes the K blocks g, g + TC_PG, .. of the CTA's sequence, so that
+//              two blocks are split at a time.  Thread p of a group owns row p of the tile: its 128-byte slice of
+//              each of the group's K blocks is prefetched TC_RAW blocks ahead with cp.async into the group's padded
+//              raw ring (no registers held), then split into tf32 hi / lo and written with tcgen05.st into the
+//              stage's A columns of TMEM (row p = TMEM lane p); the group's thread 0 also fetches the stage's B hi /
+//              lo blocks into shared memory with two 16 KB cp.async.bulk copies (no multicast).
+//   epilogue   TC_EPW warps: tcgen05.ld 32x32b of the finished accumulator (warp w reads TMEM lanes 32 (w % 4) ..,
+//              one row per lane; with 8 warps each takes two of the four 32-column chunks), row scale 1 / (rho + 1),
+//              a transpose through shared memory so that the stores (and the loads of the previous values when
+//              accumulating, eight in flight per lane) are full 128-byte row segments; then release the accumulator.
+//   last warp  barrier init, TMEM allocation (two 128-column accumulators + 64 A columns per stage) and, on
 //              lane 0, the MMA issue: 12 tcgen05.mma kind::tf32 (M = N = 128, K = 8, A from TMEM, B from shared
 //              memory) per K block, tcgen05.commit -> stage-empty barrier, and after a tile's last block ->
-//              accumulator-full barrier.  With A in TMEM the MMAs read half the shared-memory bytes (49.5 against
-//              54.4 ms of node GEMMs per 1.03M-atom evaluation with A staged in shared memory, MB_TC_A_TMEM = 0);
-//              deeper stage / raw rings (3 or 4 stages, 6 raw blocks) measured the same.
-//   warps 4-7  epilogue: tcgen05.ld 32x32b of the finished accumulator (warp w reads TMEM lanes 32 (w % 4) ..,
-//              one row per lane), row scale 1 / (rho + 1), then a transpose through shared memory so that the
-//              optional accumulate load and the store of every 32-column chunk go out as full 128-byte row
-//              segments (4 rows per warp instruction); then release the accumulator.
+//              accumulator-full barrier.
+// Measured on the 1.03M-atom evaluation (node GEMMs per evaluation): A staged in shared memory beside B, 4 producer
+// and 4 epilogue warps 54.4 ms (each MMA then reads 8 KB of operands from shared memory, about what the SM's shared
+// memory delivers at the MMA's rate); A in TMEM 49.5-50.1 ms, where a clock64 trace showed the epilogue (about
+// 11k cycles per tile) and the serial split chain of each producer warp (1.3-2.5k cycles per K block) as the
+// limits; per-lane 128-byte bulk stores from the epilogue 51.2 ms (the bulk-copy issue took ~2.5k cycles per chunk).
 // The two accumulators let a tile's epilogue overlap the next tile's K loop.  Every mbarrier wait is bounded: on
 // expiry the kernel records MB_ST_TC_TIMEOUT, every role stops, outstanding copies and MMAs are drained (bounded),
 // the TMEM is freed and the kernel exits (outputs of unfinished tiles are not written).
@@ -35,33 +39,33 @@ constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 4;          // 16 KB: one operand 
 #define MB_TC_STAGES 2
 #endif
 #ifndef MB_TC_RAW
-#define MB_TC_RAW 4
+#define MB_TC_RAW 3
 #endif
-constexpr int TC_STAGES = MB_TC_STAGES;                    // operand stages
-// A hi / lo of a stage: in TMEM (MB_TC_A_TMEM = 1; the MMA reads A from TMEM and only B from shared memory) or in
-// shared memory beside B (0)
-#ifndef MB_TC_A_TMEM
-#define MB_TC_A_TMEM 1
+#ifndef MB_TC_PG
+#define MB_TC_PG 2
 #endif
-#if MB_TC_A_TMEM
+#ifndef MB_TC_EPW
+#define MB_TC_EPW 4
+#endif
+constexpr int TC_STAGES = MB_TC_STAGES;                    // operand stages (B hi / lo in shared memory, A in TMEM)
+constexpr int TC_PG = MB_TC_PG;                            // producer groups of 4 warps; group g makes K blocks g, g + TC_PG, ..
+constexpr int TC_EPW = MB_TC_EPW;                          // epilogue warps (4: all chunks each; 8: two per warp)
 constexpr int TC_STAGE_BYTES = 2 * TC_TILE_BYTES;          // B hi, B lo
 constexpr int TC_TMEM_COLS = 512;                          // two accumulators + A hi / lo (2 x 32 columns) per stage
-#else
-constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;          // A hi, A lo, B hi, B lo
-constexpr int TC_TMEM_COLS = 2 * TC_BN;
-#endif
 constexpr int TC_A_COL = 2 * TC_BN;                        // first TMEM column of the A stages
-constexpr int TC_RAW = MB_TC_RAW;                          // cp.async depth of the raw A ring, in K blocks
+constexpr int TC_RAW = MB_TC_RAW;                          // cp.async depth of each group's raw A ring, in K blocks
 constexpr int TC_RAW_ROW = 144;                            // one row's 128-byte K slice + 16 bytes of bank padding
 constexpr int TC_RAW_BYTES = TC_BM * TC_RAW_ROW;
 constexpr int TC_EPI_ROW = 33;                             // epilogue transpose: 32 floats per row + 1 (bank spread)
-constexpr int TC_EPI_BYTES = 4 * 32 * TC_EPI_ROW * 4;      // one 32-row x 32-column chunk per epilogue warp
-constexpr int TC_THREADS = 288;                            // 4 producer warps, 4 epilogue warps, 1 MMA warp
-constexpr int TC_MMA_WARP = 8;
-static_assert(!MB_TC_A_TMEM || TC_A_COL + TC_STAGES * 2 * TC_BK <= TC_TMEM_COLS, "TMEM columns");
+constexpr int TC_EPI_WARP_BYTES = 32 * TC_EPI_ROW * 4;     // one 32-row x 32-column chunk per epilogue warp
+constexpr int TC_EPI_WARP0 = 4 * TC_PG;                    // first epilogue warp
+constexpr int TC_MMA_WARP = TC_EPI_WARP0 + TC_EPW;
+constexpr int TC_THREADS = 32 * (TC_MMA_WARP + 1);
+static_assert(TC_EPW == 4 || TC_EPW == 8, "epilogue warps");
+static_assert(TC_A_COL + TC_STAGES * 2 * TC_BK <= TC_TMEM_COLS, "TMEM columns");
 constexpr int TC_RAW_OFF = TC_STAGES * TC_STAGE_BYTES;
-constexpr int TC_EPI_OFF = TC_RAW_OFF + TC_RAW * TC_RAW_BYTES;
-constexpr int TC_BAR_OFF = TC_EPI_OFF + TC_EPI_BYTES;
+constexpr int TC_EPI_OFF = TC_RAW_OFF + TC_PG * TC_RAW * TC_RAW_BYTES;
+constexpr int TC_BAR_OFF = TC_EPI_OFF + TC_EPW * TC_EPI_WARP_BYTES;
 constexpr int TC_SMEM = TC_BAR_OFF + 256 + 1024;           // + barriers / TMEM slot / flag + alignment slack
 static_assert(TC_SMEM <= 227 * 1024, "shared memory per CTA");
 // Every mbarrier wait gives up after g_tc_wait_ns nanoseconds of %globaltimer (default 2 s; a GEMM tile takes
@@ -86,12 +90,6 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-// SWIZZLE_128B K-major canonical layout: 8-row groups of 1024 B, row r at (r % 8) * 128 inside its group, 16-byte
-// chunk c stored at chunk position c ^ (r % 8).
-__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
-  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
 // UMMA shared-memory descriptor (sm_100): start >> 4 in [0,14), LBO (unused for swizzled K-major, 1) in [16,30),
 // SBO = 1024 B between 8-row groups in [32,46), version 1 in [46,48), layout SWIZZLE_128B = 2 in [61,64).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -109,16 +107,9 @@ __host__ __device__ constexpr uint32_t tf32_idesc(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-
-// the same with A read from TMEM (tmem_a: lane 0 and the first of the 8 columns of this K step, one row per lane)
+// One MMA, A read from TMEM (tmem_a: lane 0 and the first of the 8 columns of this K step, one row per lane), B from
+// a SWIZZLE_128B K-major shared-memory image (8-row groups of 1024 B, row r at (r % 8) * 128, 16-byte chunk c at
+// chunk position c ^ (r % 8); the host writes B in that image, engine.tc_planes)
 __device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
@@ -204,14 +195,15 @@ struct TcBars {
   int failed;
 };
 
-// Row geometry of tile row `row` of global tile `tile`: problem index, A row pointer (null when out of range),
-// output row pointer and scale.
+// Row geometry of tile row `row` of global tile `tile`: problem index, K blocks, whether the row exists, and its
+// atom (through the optional order: the load is issued here, its value is only used later, by tc_a / tc_y, so
+// that the round trip overlaps other work) and component.
 struct TcRow {
   int pi;
   int nk;
-  const float* a;
-  float* y;
-  float alpha;
+  bool valid;
+  int mm;
+  int64_t at;
 };
 
 __device__ __forceinline__ TcRow tc_row(const GemmGroup& grp, int tile, int row) {
@@ -219,20 +211,48 @@ __device__ __forceinline__ TcRow tc_row(const GemmGroup& grp, int tile, int row)
   o.pi = gemm_problem_of(grp, tile);
   const GemmProblem& g = grp.p[o.pi];
   o.nk = g.nseg * (MB_C / TC_BK);
-  o.a = nullptr;
-  o.y = nullptr;
-  o.alpha = 1.f;
   const int64_t r = (int64_t)(tile - grp.tile_start[o.pi]) * TC_BM + row;
-  if (r < (int64_t)g.n_atoms * g.mult) {
+  o.valid = r < (int64_t)g.n_atoms * g.mult;
+  o.mm = 0;
+  o.at = 0;
+  if (o.valid) {
     const int64_t t = r / g.mult;
-    const int mm = (int)(r - t * g.mult);
-    const int64_t at = g.order ? g.order[t] : t;
-    o.a = g.X + at * g.ldx + (int64_t)mm * MB_C;
-    o.y = g.Y + at * g.ldy + (int64_t)(g.yoff + mm) * MB_C;
-    if (g.rho) o.alpha = 1.f / (g.rho[at] + 1.f);
+    o.mm = (int)(r - t * g.mult);
+    o.at = g.order ? (int64_t)g.order[t] : t;
   }
   return o;
 }
+
+__device__ __forceinline__ const float* tc_a(const GemmGroup& grp, const TcRow& w) {
+  const GemmProblem& g = grp.p[w.pi];
+  return w.valid ? g.X + w.at * g.ldx + (int64_t)w.mm * MB_C : nullptr;
+}
+
+__device__ __forceinline__ float* tc_y(const GemmGroup& grp, const TcRow& w) {
+  const GemmProblem& g = grp.p[w.pi];
+  return w.valid ? g.Y + w.at * g.ldy + (int64_t)(g.yoff + w.mm) * MB_C : nullptr;
+}
+
+// Cursor over this CTA's K blocks in order (tile = blockIdx.x + k gridDim.x, then kb): the tile's row geometry,
+// and the next tile's, whose order load is issued one tile ahead (tc_row).
+struct TcCursor {
+  int tile, kb;
+  TcRow rw, next;
+  __device__ __forceinline__ void init(const GemmGroup& grp, int n_tiles, int row) {
+    tile = blockIdx.x;
+    kb = 0;
+    rw = tc_row(grp, tile, row);
+    next = tile + (int)gridDim.x < n_tiles ? tc_row(grp, tile + gridDim.x, row) : rw;
+  }
+  __device__ __forceinline__ void step(const GemmGroup& grp, int n_tiles, int row) {
+    if (++kb == rw.nk) {
+      kb = 0;
+      tile += gridDim.x;
+      rw = next;
+      if (tile + (int)gridDim.x < n_tiles) next = tc_row(grp, tile + gridDim.x, row);
+    }
+  }
+};
 
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ GemmGroup grp, int n_tiles) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -254,7 +274,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&B.acc_full[a], 1);
-        mbar_init(&B.acc_empty[a], 128);
+        mbar_init(&B.acc_empty[a], 32 * TC_EPW);
       }
       B.failed = 0;
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -265,133 +285,123 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = B.tmem;
 
-  if (warp < 4) {
+  if (warp < TC_EPI_WARP0) {
     // ------------------------------------------------------------------------------------------ producers
-    const int p = tid;
-    unsigned char* raw = smem + TC_RAW_OFF;
-    // issue cursor (tile, kb) running TC_RAW blocks ahead of the split cursor; the next tile's row geometry is
-    // computed one tile early so its dependent loads (order, rho) are off the critical path
-    int it_tile = blockIdx.x, it_kb = 0;
-    TcRow it_rw = tc_row(grp, it_tile, p);
-    TcRow it_next = it_tile + (int)gridDim.x < n_tiles ? tc_row(grp, it_tile + gridDim.x, p) : it_rw;
+    // Group pg (warps 4 pg .. 4 pg + 3) makes the K blocks seq = pg, pg + TC_PG, ..; thread p of a group owns
+    // row p of the tile (TMEM lane p: warp w reaches lanes 32 (w % 4) ..).
+    const int pg = warp >> 2, p = tid & 127;
+    unsigned char* raw = smem + TC_RAW_OFF + pg * TC_RAW * TC_RAW_BYTES;
+    // issue cursor, TC_RAW of this group's blocks ahead of the consumer cursor
+    TcCursor ic, cc;
+    ic.init(grp, n_tiles, p);
+    for (int q = 0; q < pg; ++q) ic.step(grp, n_tiles, p);
+    cc = ic;
     auto issue_next = [&](int slot) {
-      if (it_tile < n_tiles) {
-        if (it_rw.a) {
-          const GemmProblem& g = grp.p[it_rw.pi];
-          const int seg = (it_kb * TC_BK) / MB_C, kin = it_kb * TC_BK - seg * MB_C;
-          const float* src = it_rw.a + (int64_t)g.xoff[seg] * MB_C + kin;
+      if (ic.tile < n_tiles) {
+        if (ic.rw.valid) {
+          const GemmProblem& g = grp.p[ic.rw.pi];
+          const int seg = (ic.kb * TC_BK) / MB_C, kin = ic.kb * TC_BK - seg * MB_C;
+          const float* src = tc_a(grp, ic.rw) + (int64_t)g.xoff[seg] * MB_C + kin;
           unsigned char* dst = raw + slot * TC_RAW_BYTES + p * TC_RAW_ROW;
 #pragma unroll
           for (int q = 0; q < 8; ++q) cp_async16(dst + 16 * q, src + 4 * q);
         }
-        if (++it_kb == it_rw.nk) {
-          it_kb = 0;
-          it_tile += gridDim.x;
-          it_rw = it_next;
-          if (it_tile + (int)gridDim.x < n_tiles) it_next = tc_row(grp, it_tile + gridDim.x, p);
-        }
+        for (int q = 0; q < TC_PG; ++q) ic.step(grp, n_tiles, p);
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
 #pragma unroll 1
     for (int q = 0; q < TC_RAW; ++q) issue_next(q);
-    int seq = 0;                                   // K blocks consumed (stage / phase counter)
-    TcRow rw = tc_row(grp, blockIdx.x, p);
+    int last_b[TC_STAGES];                          // last seq whose B copies this thread issued, per stage
+#pragma unroll
+    for (int s = 0; s < TC_STAGES; ++s) last_b[s] = -1;
     // every exit decision is warp-uniform: the loop body holds warp-collective tcgen05.st.sync.aligned
-    for (int tile = blockIdx.x; tile < n_tiles && !__shfl_sync(0xffffffffu, *failed, 0); tile += gridDim.x) {
-      const GemmProblem& g = grp.p[rw.pi];
-      const int nk = rw.nk;
-      const bool have = rw.a != nullptr;
-      for (int kb = 0; kb < nk; ++kb, ++seq) {
-        const int s = seq % TC_STAGES, slot = seq % TC_RAW;
-        asm volatile("cp.async.wait_group %0;" ::"n"(TC_RAW - 1) : "memory");
-        float4 v[8];
-        const unsigned char* src = raw + slot * TC_RAW_BYTES + p * TC_RAW_ROW;
+    for (int seq = pg, j = 0; cc.tile < n_tiles; seq += TC_PG, ++j) {
+      if (__shfl_sync(0xffffffffu, *failed, 0)) break;
+      const int s = seq % TC_STAGES, slot = j % TC_RAW, kb = cc.kb;
+      const GemmProblem& g = grp.p[cc.rw.pi];
+      const bool have = cc.rw.valid;
+      asm volatile("cp.async.wait_group %0;" ::"n"(TC_RAW - 1) : "memory");
+      float4 v[8];
+      const unsigned char* src = raw + slot * TC_RAW_BYTES + p * TC_RAW_ROW;
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          v[q] = have ? *reinterpret_cast<const float4*>(src + 16 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        issue_next(slot);                          // the slot has been read: refill it TC_RAW blocks ahead
-#if MB_TC_A_TMEM
-        uint32_t ahi[32], alo[32];                 // split before the wait, so that the wait covers it
+      for (int q = 0; q < 8; ++q)
+        v[q] = have ? *reinterpret_cast<const float4*>(src + 16 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      issue_next(slot);                            // the slot has been read: refill it TC_RAW blocks ahead
+      uint32_t ahi[32], alo[32];                   // split before the wait, so that the wait covers it
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float c4[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+      for (int q = 0; q < 8; ++q) {
+        const float c4[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float h = tf32_rna(c4[j]);
-            ahi[4 * q + j] = __float_as_uint(h);
-            alo[4 * q + j] = __float_as_uint(tf32_rna(c4[j] - h));
-          }
+        for (int k = 0; k < 4; ++k) {
+          const float h = tf32_rna(c4[k]);
+          ahi[4 * q + k] = __float_as_uint(h);
+          alo[4 * q + k] = __float_as_uint(tf32_rna(c4[k] - h));
         }
-#endif
-        // stage s free once the MMAs of its previous use completed (first use: the preceding phase counts done)
-        if (!__all_sync(0xffffffffu, mbar_wait(&B.empty[s], ((seq / TC_STAGES) & 1) ^ 1))) {
-          *failed = 1;
-          break;
-        }
-        unsigned char* st = smem + s * TC_STAGE_BYTES;
-        if (p == 0) {
-          const int seg = (kb * TC_BK) / MB_C, kin = kb * TC_BK - seg * MB_C;
-          const float* bsrc = g.B + (int64_t)seg * MB_C * MB_C + (int64_t)(kin / TC_BK) * (TC_BM * TC_BK);
-          mbar_arrive_tx(&B.bfull[s], 2 * TC_TILE_BYTES);
-          bulk_g2s(st + TC_STAGE_BYTES - 2 * TC_TILE_BYTES, bsrc, TC_TILE_BYTES, &B.bfull[s]);
-          bulk_g2s(st + TC_STAGE_BYTES - TC_TILE_BYTES, bsrc + g.plane, TC_TILE_BYTES, &B.bfull[s]);
-        }
-#if MB_TC_A_TMEM
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(TC_A_COL + s * 2 * TC_BK);
-        tmem_st32(ta, ahi);
-        tmem_st32(ta + TC_BK, alo);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-#else
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 hi, lo;
-          hi.x = tf32_rna(v[q].x); lo.x = tf32_rna(v[q].x - hi.x);
-          hi.y = tf32_rna(v[q].y); lo.y = tf32_rna(v[q].y - hi.y);
-          hi.z = tf32_rna(v[q].z); lo.z = tf32_rna(v[q].z - hi.z);
-          hi.w = tf32_rna(v[q].w); lo.w = tf32_rna(v[q].w - hi.w);
-          const uint32_t off = sw128_offset(p, q);
-          *reinterpret_cast<float4*>(st + off) = hi;
-          *reinterpret_cast<float4*>(st + TC_TILE_BYTES + off) = lo;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-#endif
-        // test hook (off unless mace_b200_tc_test_hooks armed it): one arrival of CTA 0's first K block goes missing
-        const bool skip = seq == 0 && p == 0 && blockIdx.x == 0 && *(volatile int*)&g_tc_skip_arrival &&
-                          atomicExch(&g_tc_skip_arrival, 0);
-        if (!skip) mbar_arrive(&B.full[s]);
       }
-      if (tile + (int)gridDim.x < n_tiles) rw = tc_row(grp, tile + gridDim.x, p);
+      // stage s free once the MMAs of its previous use completed (first use: the preceding phase counts done)
+      if (!__all_sync(0xffffffffu, mbar_wait(&B.empty[s], ((seq / TC_STAGES) & 1) ^ 1))) {
+        *failed = 1;
+        break;
+      }
+      if (p == 0) {
+        unsigned char* st = smem + s * TC_STAGE_BYTES;
+        const int seg = (kb * TC_BK) / MB_C, kin = kb * TC_BK - seg * MB_C;
+        const float* bsrc = g.B + (int64_t)seg * MB_C * MB_C + (int64_t)(kin / TC_BK) * (TC_BM * TC_BK);
+        mbar_arrive_tx(&B.bfull[s], 2 * TC_TILE_BYTES);
+        bulk_g2s(st, bsrc, TC_TILE_BYTES, &B.bfull[s]);
+        bulk_g2s(st + TC_TILE_BYTES, bsrc + g.plane, TC_TILE_BYTES, &B.bfull[s]);
+        last_b[s] = seq;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(TC_A_COL + s * 2 * TC_BK);
+      tmem_st32(ta, ahi);
+      tmem_st32(ta + TC_BK, alo);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      // test hook (off unless mace_b200_tc_test_hooks armed it): one arrival of CTA 0's first K block goes missing
+      const bool skip = seq == 0 && p == 0 && blockIdx.x == 0 && *(volatile int*)&g_tc_skip_arrival &&
+                        atomicExch(&g_tc_skip_arrival, 0);
+      if (!skip) mbar_arrive(&B.full[s]);
+      for (int q = 0; q < TC_PG; ++q) cc.step(grp, n_tiles, p);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     // after a timeout: B copies this thread issued may still be landing in the stages
     if (p == 0 && *failed)
-      for (int s = 0; s < TC_STAGES; ++s) {
-        const int last = seq - 1 - ((seq - 1 - s) % TC_STAGES + TC_STAGES) % TC_STAGES;   // last seq using stage s
-        if (last >= 0) mbar_wait(&B.bfull[s], (last / TC_STAGES) & 1);
-      }
+      for (int s = 0; s < TC_STAGES; ++s)
+        if (last_b[s] >= 0) mbar_wait(&B.bfull[s], (last_b[s] / TC_STAGES) & 1);
   } else if (warp < TC_MMA_WARP) {
     // ------------------------------------------------------------------------------------------ epilogue
-    const int q4 = warp & 3, row = q4 * 32 + lane;
+    // Warp w reads TMEM lanes 32 (w % 4) .. (one tile row per lane) and handles the 32-column chunks
+    // h = (w - TC_EPI_WARP0) / 4, + TC_EPW / 4, ..; each chunk is transposed through shared memory so that the
+    // output stores (and, when accumulating, the loads of the previous values, all eight issued together) are full
+    // 128-byte row segments, 4 rows per warp instruction.
+    const int q4 = warp & 3, row = q4 * 32 + lane, e = warp - TC_EPI_WARP0;
+    float* stg = reinterpret_cast<float*>(smem + TC_EPI_OFF + e * TC_EPI_WARP_BYTES);
+    // lane l stores rows 4 i + l / 8 (i = 0..7), columns 4 (l % 8) .. + 3 of the chunk
+    const int srow = lane >> 3, scol = (lane & 7) * 4;
     int tc = 0;
     // every exit decision is warp-uniform: the loop body holds warp-collective tcgen05.ld.sync.aligned
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tc) {
       if (__shfl_sync(0xffffffffu, *failed, 0)) break;
       const int a = tc & 1;
       const TcRow rw = tc_row(grp, tile, row);     // its loads overlap the wait
+      const GemmProblem& g = grp.p[rw.pi];
+      float* y = tc_y(grp, rw);
+      const float rho = (rw.valid && g.rho) ? g.rho[rw.at] : 0.f;
+      float* yr[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        yr[i] = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(y), 4 * i + srow));
       if (!__all_sync(0xffffffffu, mbar_wait(&B.acc_full[a], (tc >> 1) & 1))) {
         *failed = 1;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int acc = grp.p[rw.pi].accumulate;
-      float* stg = reinterpret_cast<float*>(smem + TC_EPI_OFF) + q4 * 32 * TC_EPI_ROW;   // this warp's chunk
-      // lane l stores rows 4 i + l / 8 (i = 0..7), columns 4 (l % 8) .. + 3 of the chunk: 4 rows per instruction
-      const int srow = lane >> 3, scol = (lane & 7) * 4;
+      const bool acc = g.accumulate != 0;
+      const float alpha = 1.f / (rho + 1.f);
 #pragma unroll 1
-      for (int h = 0; h < 4; ++h) {
+      for (int h = e >> 2; h < 4; h += TC_EPW / 4) {
         uint32_t x[32];
         const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(a * TC_BN + 32 * h);
         asm volatile(
@@ -402,25 +412,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
               "=r"(x[16]), "=r"(x[17]), "=r"(x[18]), "=r"(x[19]), "=r"(x[20]), "=r"(x[21]), "=r"(x[22]), "=r"(x[23]),
               "=r"(x[24]), "=r"(x[25]), "=r"(x[26]), "=r"(x[27]), "=r"(x[28]), "=r"(x[29]), "=r"(x[30]), "=r"(x[31])
             : "r"(taddr));
+        float4 prev[8];
+        if (acc) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            prev[i] = yr[i] ? *reinterpret_cast<const float4*>(yr[i] + 32 * h + scol) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         __syncwarp();                                // the previous chunk's reads of the staging area are done
 #pragma unroll
-        for (int j = 0; j < 32; ++j) stg[lane * TC_EPI_ROW + j] = __uint_as_float(x[j]) * rw.alpha;
+        for (int k = 0; k < 32; ++k) stg[lane * TC_EPI_ROW + k] = __uint_as_float(x[k]) * alpha;
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int r = 4 * i + srow;                // row of this warp's 32 (lane r of the TMEM load)
-          float* yrow = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(rw.y), r));
-          if (yrow) {
-            const float* sv = stg + r * TC_EPI_ROW + scol;
-            float4 o = make_float4(sv[0], sv[1], sv[2], sv[3]);
-            float4* yp = reinterpret_cast<float4*>(yrow + 32 * h + scol);
-            if (acc) {
-              const float4 p4 = *yp;
-              o.x += p4.x; o.y += p4.y; o.z += p4.z; o.w += p4.w;
-            }
-            *yp = o;
+          const float* sv = stg + (4 * i + srow) * TC_EPI_ROW + scol;
+          float4 o = make_float4(sv[0], sv[1], sv[2], sv[3]);
+          if (acc) {
+            o.x += prev[i].x; o.y += prev[i].y; o.z += prev[i].z; o.w += prev[i].w;
           }
+          if (yr[i]) *reinterpret_cast<float4*>(yr[i] + 32 * h + scol) = o;
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -450,8 +460,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t d = tmem + (uint32_t)(a * TC_BN);
-        const uint32_t b_hi = smem_u32(smem + (s + 1) * TC_STAGE_BYTES - 2 * TC_TILE_BYTES), b_lo = b_hi + TC_TILE_BYTES;
-#if MB_TC_A_TMEM
+        const uint32_t b_hi = smem_u32(smem + s * TC_STAGE_BYTES), b_lo = b_hi + TC_TILE_BYTES;
         const uint32_t a_hi = tmem + (uint32_t)(TC_A_COL + s * 2 * TC_BK), a_lo = a_hi + TC_BK;
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 8; ++kk) {
@@ -460,16 +469,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
           mma_tf32_ts(d, a_hi + 8 * kk, sw128_desc(b_lo + ko), idesc, 1u);
           mma_tf32_ts(d, a_lo + 8 * kk, sw128_desc(b_hi + ko), idesc, 1u);
         }
-#else
-        const uint32_t a_hi = smem_u32(smem + s * TC_STAGE_BYTES), a_lo = a_hi + TC_TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < TC_BK / 8; ++kk) {
-          const uint32_t ko = kk * 32;               // 8 tf32 = 32 bytes along K inside the swizzle atom
-          mma_tf32(d, sw128_desc(a_hi + ko), sw128_desc(b_hi + ko), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          mma_tf32(d, sw128_desc(a_hi + ko), sw128_desc(b_lo + ko), idesc, 1u);
-          mma_tf32(d, sw128_desc(a_lo + ko), sw128_desc(b_hi + ko), idesc, 1u);
-        }
-#endif
         mma_commit(&B.empty[s]);
         last_bar = &B.empty[s];
         last_par = ph;
