@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define MB_ABI_VERSION 3
+#define MB_ABI_VERSION 4
 
 enum {
   MB_OK = 0,
@@ -62,14 +62,15 @@ typedef struct {
   const float* Wp1;            /* [2][C][C]     products[0].linear per l */
   const float* Wp1T;
   const float* wr0;            /* [C]           readouts[0] */
-  const float* sc1;            /* [S][NT1][C]   symmetric contraction 1 (L = 0 and L = 1 outputs) */
+  const float* sc1;            /* [S][NT1/4][C][4]  symmetric contraction 1 (L = 0 and L = 1 outputs); coefficient t of
+                                  channel c at [t / 4][c][t % 4], NT1 rounded up to a multiple of 4 with zeros */
   const float* Wup2;           /* [2][C][C]     interactions[1].linear_up per l */
   const float* Wup2T;
   const float* Wsk1;           /* [S][C][C]     interactions[1].skip_tp (0e -> 0e) per species */
   const float* Wsk1T;
   const float* Wlin2;          /* [10][C][C]    interactions[1].linear per mid entry (scaled by its group) */
   const float* Wlin2T;
-  const float* sc2;            /* [S][NT2][C]   symmetric contraction 2 (L = 0) */
+  const float* sc2;            /* [S][NT2/4][C][4]  symmetric contraction 2 (L = 0), same layout */
   const float* Wp2;            /* [C][C]        products[1].linear */
   const float* Wp2T;
   const float* W1r;            /* [C][16]       readouts[1].linear_1 / sqrt(C) */

@@ -122,14 +122,15 @@ int gemm_launch(const float* X, int64_t ldx, const int32_t* xoff, int nseg, cons
 }
 
 // ------------------------------------------------------------------------------------------------ symmetric contraction
-// One thread per channel.  x [n][16][C]; block 0 -> A [n][4][C], block 1 -> A [n][C].  A CTA takes K atoms of one
+// One thread per channel.  x [n][16][C]; block 0 -> A [n][4][C], block 1 -> A [n][C]; coefficients
+// [S][NT4][C][4] (coefficient t of channel c at [t / 4][c][t % 4], 16-byte loads).  A CTA takes K atoms of one
 // species (consecutive entries of a species-sorted row list; the per-species coefficients are then loaded once for
 // all K atoms) or, with a per-atom species array, one atom (K = 1).
 template <int BLK, int K>
 __global__ void __launch_bounds__(128) k_symcon_fwd(const float* __restrict__ coef, const float* __restrict__ x,
                                                     float* __restrict__ A, const int* __restrict__ rows, int n,
                                                     const int* __restrict__ spec, int s0, int S) {
-  constexpr int NT = BLK == 0 ? SC0_NT : SC1_NT;
+  constexpr int NT4 = BLK == 0 ? SC0_NT4 : SC1_NT4;
   constexpr int NO = BLK == 0 ? SC0_NOUT : SC1_NOUT;
   const int c = threadIdx.x;
   int ri[K];
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(128) k_symcon_fwd(const float* __restrict__ co
 #pragma unroll
     for (int q = 0; q < 16; ++q) xv[a][q] = ri[a] >= 0 ? xp[q * MB_C] : 0.f;
   }
-  const float* cf = coef + (size_t)s * NT * MB_C + c;
+  const float4* cf = reinterpret_cast<const float4*>(coef) + (size_t)s * NT4 * MB_C + c;
   if constexpr (BLK == 0)
     sc0_fwd<K>(xv, cf, out);
   else
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(128) k_symcon_bwd(const float* __restrict__ co
                                                     const int* __restrict__ rows, int n, const int* __restrict__ spec,
                                                     int s0, int S, const float* __restrict__ rho,
                                                     float* __restrict__ grho) {
-  constexpr int NT = BLK == 0 ? SC0_NT : SC1_NT;
+  constexpr int NT4 = BLK == 0 ? SC0_NT4 : SC1_NT4;
   constexpr int NO = BLK == 0 ? SC0_NOUT : SC1_NOUT;
   __shared__ float red[K][4];
   const int c = threadIdx.x;
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(128) k_symcon_bwd(const float* __restrict__ co
 #pragma unroll
     for (int q = 0; q < NO; ++q) ga[a][q] = ri[a] >= 0 ? gp[q * MB_C] : 0.f;
   }
-  const float* cf = coef + (size_t)s * NT * MB_C + c;
+  const float4* cf = reinterpret_cast<const float4*>(coef) + (size_t)s * NT4 * MB_C + c;
   if constexpr (BLK == 0)
     sc0_bwd<K>(xv, cf, ga, gv);
   else

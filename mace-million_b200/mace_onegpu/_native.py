@@ -16,7 +16,7 @@ c_i32, c_i64, c_u32, c_u64, c_f32, c_f64 = (ctypes.c_int32, ctypes.c_int64, ctyp
 c_vp = ctypes.c_void_p
 
 
-ABI_VERSION = 3          # MB_ABI_VERSION of include/mace_b200.h this binding mirrors
+ABI_VERSION = 4          # MB_ABI_VERSION of include/mace_b200.h this binding mirrors
 ST_UNSORTED = 64         # MB_ST_UNSORTED
 
 

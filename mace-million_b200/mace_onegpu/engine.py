@@ -160,6 +160,17 @@ def fold_weights(model: Mdl.MACEModel, cols) -> dict:
 L1_DENSITY_H = 64      # radial-MLP hidden width the density kernels are written for (2 species slots x 64 = C)
 
 
+def sc_coef_layout(sc) -> np.ndarray:
+    """Symmetric-contraction coefficients [S][NT][C] -> [S][ceil(NT / 4)][C][4] (zero padded): coefficient t of
+    channel c at [t // 4][c][t % 4], so that the kernels load four consecutive coefficients per 16-byte load."""
+    sc = np.asarray(sc, dtype=np.float64)
+    S, nt, c = sc.shape
+    nt4 = (nt + 3) // 4
+    pad = np.zeros((S, nt4 * 4, c))
+    pad[:, :nt] = sc
+    return np.ascontiguousarray(pad.reshape(S, nt4, 4, c).transpose(0, 1, 3, 2))
+
+
 def l1_density_supported(f: dict) -> bool:
     """The density-projection layer 1 keeps up to two species slots of 64 hidden features per receiver (K = C)."""
     return f["S"] <= 2 and f["A0"][3].shape[0] == L1_DENSITY_H
@@ -233,14 +244,14 @@ class FoldedModel:
         t["Wp1"] = _f32(f["Wp1"], dev)
         t["Wp1T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wp1"], -1, -2)), dev)
         t["wr0"] = _f32(f["wr0"], dev)
-        t["sc1"] = _f32(f["sc0"], dev)
+        t["sc1"] = _f32(sc_coef_layout(f["sc0"]), dev)
         t["Wup2"] = _f32(f["Wup2"], dev)
         t["Wup2T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wup2"], -1, -2)), dev)
         t["Wsk1"] = _f32(f["Wsk1"], dev)
         t["Wsk1T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wsk1"], -1, -2)), dev)
         t["Wlin2"] = _f32(f["Wlin2"], dev)
         t["Wlin2T"] = _f32(np.ascontiguousarray(np.swapaxes(f["Wlin2"], -1, -2)), dev)
-        t["sc2"] = _f32(f["sc1"], dev)
+        t["sc2"] = _f32(sc_coef_layout(f["sc1"]), dev)
         t["Wp2"] = _f32(f["Wp2"], dev)
         t["Wp2T"] = _f32(np.ascontiguousarray(f["Wp2"].T), dev)
         t["W1r"] = _f32(f["W1r"], dev)
