@@ -369,6 +369,39 @@ class Plan:
         return Plan(eng, *self._inputs, self.nl, self.nt, stream_host=False)
 
 
+def pipeline_steps(nch: int, chunk: int, nl: int, largest_sender, lookahead: int = 2):
+    """Order of the pipelined pass A / pass B schedule of a streamed pair list (ThreePassEngine._run_pipelined).
+    Pass-B chunk c reads the X2 rows of its senders only, so it can run once pass A (and the X2 GEMM of its rows)
+    has covered the chunks up to need(c) = max(c, largest sender of c // chunk); a chunk with a ghost sender
+    (index >= nl) needs the H1 exchange, which follows the last pass-A chunk.  largest_sender(c) is -1 for a chunk
+    without pairs and may block until the chunk has arrived: it is called for chunk k - lookahead + 1 right after
+    pass-A chunk k is issued (the host stays `lookahead` chunks ahead of the arrivals), then for the rest.
+    Yields ("A", k), ("early_B", c) for a pass-B chunk issued before the last pass-A chunk, ("exchange", None)
+    once after the last pass-A chunk, and ("B", c) for the others.  With spatially sorted atoms (LAMMPS sorts them
+    into bins) need(c) is c + 2 or c + 3 for almost every chunk, so the pair list's host-to-device transfer hides
+    under pass B instead of under pass A alone."""
+    pend = []                 # heap of (need, chunk) for chunks whose sender range is known
+    known = 0
+
+    def learn(upto):
+        nonlocal known
+        while known < upto:
+            hi = int(largest_sender(known))
+            need = known if hi < 0 else nch if hi >= nl else max(known, hi // chunk)
+            heapq.heappush(pend, (need, known))
+            known += 1
+
+    for k in range(nch):
+        yield "A", k
+        learn(max(0, k + 1 - lookahead))
+        while pend and pend[0][0] <= k:
+            yield ("early_B" if k < nch - 1 else "B"), heapq.heappop(pend)[1]
+    yield "exchange", None
+    learn(nch)
+    while pend:
+        yield "B", heapq.heappop(pend)[1]
+
+
 def _pinned(t, dtype) -> bool:
     return isinstance(t, torch.Tensor) and not t.is_cuda and t.is_pinned() and t.dtype == dtype and t.is_contiguous()
 
@@ -553,16 +586,10 @@ class ThreePassEngine:
     _LOOKAHEAD = 2      # pipelined schedule: pass A chunk k is issued once chunk k - 2's sender range is known
 
     def _run_pipelined(self, plan, ev, b, dep_host, ready, forward_exchange=None, reverse_exchange=None):
-        """Evaluation of a streamed pair list with pass B interleaved into pass A.  Pass-B chunk c reads the X2 rows
-        of its senders only, so it can run once pass A (and the X2 GEMM) has covered the chunks up to
-        need(c) = max(c, largest sender of c // chunk); the side stream reports each chunk's sender range
-        (mace_b200_sender_range) together with its arrival, and the host issues, after pass-A chunk k, every known
-        chunk with need(c) <= k.  A chunk with a ghost sender (index >= nlocal) waits for the H1 forward exchange,
-        which follows the last pass-A chunk as in _run.  With spatially sorted atoms (LAMMPS sorts them into bins;
-        a domain ordered interior first, domain.Decomposition), need(c) is c + 2 or c + 3 for almost every chunk
-        without ghost senders, so the pair list's host-to-device transfer hides under pass B instead of under pass
-        A alone.  Pass C follows all of pass B.  Timing marks: t_A covers pass A with the pass-B chunks interleaved
-        in it, t_B the remaining pass-B chunks and the G1 fold."""
+        """Evaluation of a streamed pair list with pass B interleaved into pass A (the order: pipeline_steps).  The
+        side stream reports each chunk's sender range (mace_b200_sender_range) together with its arrival; the host
+        reads a chunk's largest sender once the chunk has arrived.  Pass C follows all of pass B.  Timing marks: t_A
+        covers pass A with the pass-B chunks interleaved in it, t_B the remaining pass-B chunks and the G1 fold."""
         L = N.lib()
         m = N.byref(self.fm.struct)
         evp = N.byref(ev)
@@ -578,40 +605,27 @@ class ThreePassEngine:
         marks = self._pass_marks() if self.pass_timing else None
         self._marks_valid = marks is not None
         mark = (lambda k: marks[k].record()) if marks else (lambda k: None)
-        pend = []                 # heap of (need, chunk) for chunks whose sender range is known
-        known = 0
 
-        def learn(upto):
-            nonlocal known
-            while known < upto:
-                ready[known].synchronize()
-                hi = int(dep_host[known, 1])
-                need = known if hi < 0 else nch if hi >= nl else max(known, hi // C_)
-                heapq.heappush(pend, (need, known))
-                known += 1
-
-        def run_b(c):
-            N.check(L.mace_b200_pass_b_chunks(m, evp, c, c + 1, st), "pass_b")
+        def largest_sender(c):
+            ready[c].synchronize()
+            return int(dep_host[c, 1])
 
         mark(0)
-        early = 0
-        for k in range(nch):
-            N.check(L.mace_b200_pass_a_chunks(m, evp, k, k + 1, st), "pass_a")
-            N.check(L.mace_b200_x2_rows(m, evp, k * C_, min((k + 1) * C_, nl), st), "x2_rows")
-            learn(max(0, k + 1 - self._LOOKAHEAD))
-            while pend and pend[0][0] <= k:
-                run_b(heapq.heappop(pend)[1])
-                early += k < nch - 1
-        self.early_b_chunks = early
-        mark(1)
-        if plan.nt > nl:
-            if forward_exchange is not None:
-                forward_exchange(b["H1"].view(plan.nt, 4 * C))
-            N.check(L.mace_b200_x2_rows(m, evp, nl, plan.nt, st), "x2_rows")
-        mark(2)
-        learn(nch)
-        while pend:
-            run_b(heapq.heappop(pend)[1])
+        self.early_b_chunks = 0
+        for kind, k in pipeline_steps(nch, C_, nl, largest_sender, self._LOOKAHEAD):
+            if kind == "A":
+                N.check(L.mace_b200_pass_a_chunks(m, evp, k, k + 1, st), "pass_a")
+                N.check(L.mace_b200_x2_rows(m, evp, k * C_, min((k + 1) * C_, nl), st), "x2_rows")
+            elif kind == "early_B" or kind == "B":
+                N.check(L.mace_b200_pass_b_chunks(m, evp, k, k + 1, st), "pass_b")
+                self.early_b_chunks += kind == "early_B"
+            else:                                   # "exchange": after the last pass-A chunk
+                mark(1)
+                if plan.nt > nl:
+                    if forward_exchange is not None:
+                        forward_exchange(b["H1"].view(plan.nt, 4 * C))
+                    N.check(L.mace_b200_x2_rows(m, evp, nl, plan.nt, st), "x2_rows")
+                mark(2)
         N.check(L.mace_b200_fold_g1(m, evp, 0, plan.nt, st), "fold_g1")
         mark(3)
         if reverse_exchange is not None and plan.nt > nl:
