@@ -33,22 +33,48 @@ _RUNTIME = ("_eng", "_dev", "_cols", "_log", "_fmax_abort", "_t_end")
 _INT_MAX = 2 ** 31 - 1
 
 
-def _exchange(fn, src, dst, D):
-    """LAMMPS' ML-IAP comm buffers are sized with 32-bit ints (ntotal * D): split the feature columns so that every
-    call stays below 2^31 elements (mace_onegpu/mliap_threepass.py:40-55)."""
-    nt = src.shape[0]
+def exchange_blocks(nt: int, D: int):
+    """Column blocks (first column, width) of one exchange of an [nt, D] feature array.  LAMMPS' ML-IAP comm
+    buffers are sized with 32-bit ints (ntotal * D), so every callback must move fewer than 2^31 - 1 elements: the
+    width is D >> k for the smallest k that satisfies this (at least 1 column), the blocks tile [0, D) in order and
+    the last one may be narrower.  This is the call pattern of the reference's _exchange
+    (mace_onegpu/mliap_threepass.py:40-55), which halves the width until it fits."""
     if nt * D < _INT_MAX:
+        return [(0, D)]
+    k = 0
+    while (D >> k) > 1 and nt * (D >> k) >= _INT_MAX:
+        k += 1
+    w = D >> k
+    return [(c0, min(w, D - c0)) for c0 in range(0, D, w)]
+
+
+def _exchange(fn, src, dst, D):
+    """dst = fn applied to src, one callback per column block of exchange_blocks (blocks narrower than D go through
+    contiguous copies: the callback sees a dense [nt, width] array)."""
+    blocks = exchange_blocks(int(src.shape[0]), D)
+    if len(blocks) == 1:
         fn(src, dst, D)
         return
-    w = D
-    while nt * w >= _INT_MAX and w > 1:
-        w //= 2
-    for c in range(0, D, w):
-        cw = min(w, D - c)
-        s = src[:, c:c + cw].contiguous()
-        d = torch.empty_like(s)
-        fn(s, d, cw)
-        dst[:, c:c + cw] = d
+    for c0, w in blocks:
+        part_in = src[:, c0:c0 + w].contiguous()
+        part_out = torch.empty_like(part_in)
+        fn(part_in, part_out, w)
+        dst[:, c0:c0 + w] = part_out
+
+
+def neighbour_slot_guard(nl: int, P: int, r_max: float):
+    """Refuse a call whose LAMMPS neighbour list would approach 2^31 slots (mace_onegpu/mliap_threepass.py:450-461):
+    Kokkos indexes the full list, pairs inside r_max grown by the skin shell, with 32-bit ints, and an overflow there
+    is an illegal device access inside LAMMPS.  Estimate P ((r_max + skin) / r_max)^3 against 0.95 * 2^31, skin from
+    MACE3P_SKIN (2 A); MACE3P_ALLOW_HUGE=1 lifts the refusal.  The message is the reference's."""
+    if os.environ.get("MACE3P_ALLOW_HUGE", "0") == "1":
+        return
+    skin = float(os.environ.get("MACE3P_SKIN", "2.0"))
+    est_slots = P * ((r_max + skin) / r_max) ** 3
+    if est_slots > 0.95 * 2 ** 31:
+        raise RuntimeError(f"ThreePassMLIAP guard: nlocal={nl:,}, pairs={P:,} -> estimated LAMMPS neighbour slots "
+                           f"{est_slots:.3e} is close to the 2^31 int32 limit of the Kokkos neighbour list "
+                           f"(skin {skin} A). Use fewer atoms per GPU, a smaller skin, or more GPUs.")
 
 
 class ThreePassMLIAP(MLIAPUnified):
@@ -104,15 +130,8 @@ class ThreePassMLIAP(MLIAPUnified):
         if nl == 0 or P <= 1:
             return
         t_start = time.perf_counter()
-        t_gap = (t_start - self._t_end) if getattr(self, "_t_end", None) else None
-        # int32 guard of the Kokkos neighbour list (mliap_threepass.py:450-461)
-        skin = float(os.environ.get("MACE3P_SKIN", "2.0"))
-        rmax = 2.0 * self.rcutfac
-        est_slots = P * ((rmax + skin) / rmax) ** 3
-        if est_slots > 0.95 * 2 ** 31 and os.environ.get("MACE3P_ALLOW_HUGE", "0") != "1":
-            raise RuntimeError(f"ThreePassMLIAP guard: nlocal={nl:,}, pairs={P:,} -> estimated LAMMPS neighbour slots "
-                               f"{est_slots:.3e} is close to the 2^31 int32 limit of the Kokkos neighbour list "
-                               f"(skin {skin} A). Use fewer atoms per GPU, a smaller skin, or more GPUs.")
+        prev_end = getattr(self, "_t_end", None)        # LAMMPS' time between two calls, for the per-call log
+        neighbour_slot_guard(nl, P, 2.0 * self.rcutfac)
         elems = torch.as_tensor(data.elems)
         if not hasattr(self, "_eng"):
             self._setup(elems)
@@ -158,7 +177,8 @@ class ThreePassMLIAP(MLIAPUnified):
                                             sorted_pairs=plan.perm is None, streamed_pairs=plan.host_src is not None,
                                             graphs=bool(eng.graphs), captures=eng.captures,
                                             t_total=time.perf_counter() - t_start, t_prep=t_prep, **eng.pass_times(),
-                                            t_gap_lammps=t_gap, peak_gb=peak, fmax=fmax)) + "\n")
+                                            t_gap_lammps=None if prev_end is None else t_start - prev_end,
+                                            peak_gb=peak, fmax=fmax)) + "\n")
         self._t_end = time.perf_counter()
 
     def compute_descriptors(self, data):

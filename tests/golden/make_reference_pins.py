@@ -21,6 +21,8 @@ Cases (reference code that ran, inputs, what is stored):
   fast_layers.install does, chunk 64: total energy and atom forces (original atom order).
 * ``tables``: conv_spline.build_tables (conv_spline.py:230-249) for species (H, O), 512 knots over [0.5, r_max]:
   knot rows 0, 1, 255, 510, 511 of TV and TG (fp32) of every ordered species pair, both interaction blocks.
+* ``xchg``: mliap_threepass._exchange (mliap_threepass.py:40-55) on meta tensors (no memory) of ntotal x D arrays
+  beyond 2^31 elements: the column width of each callback, in call order.
 * ``hermite``: spline_radial._hermite_eval (spline_radial.py:37-57), value and d/dr, on fp64 tables of block 1 at
   radii below the first knot, inside, on knots and near r_max (first 64 columns).
 """
@@ -46,6 +48,8 @@ import ref_adapter  # noqa: E402
 E0_SEED, SHIFT = 7, 0.25
 TABLE_ROWS = (0, 1, 255, 510, 511)
 HERMITE_COLS = 64
+XCHG_CASES = ((1000, 512), (4_194_304, 512), (9_000_000, 512), (5_000_000, 500), (7_000_000, 700),
+              (1_000_000_000, 5), (2 ** 31, 3))
 
 
 # ------------------------------------------------------------------------------------------ shared with the tests
@@ -151,6 +155,13 @@ def main(ref_root):
             out[f"tab{i}_TV"] = TV.view(P, M_, -1)[:, rows].numpy()
             out[f"tab{i}_TG"] = TG.view(P, M_, -1)[:, rows].numpy()
         out.update(tab_r_lo=np.float64(tab["r_lo"]), tab_r_hi=np.float64(tab["r_hi"]), tab_M=np.int64(M_))
+
+        xg = mod("mliap_threepass")._exchange
+        for nt_, D_ in XCHG_CASES:
+            widths = []
+            xg(lambda s_, d_, w_: widths.append((s_.shape[1], w_)), torch.empty(nt_, D_, device="meta"),
+               torch.empty(nt_, D_, device="meta"), D_)
+            out[f"xchg_{nt_}_{D_}"] = np.array(widths, dtype=np.int64)
 
         sr = mod("spline_radial")
         t = mace_ref.MaceRef(mdl.params(), arch, spline_knots=512).tables[1]

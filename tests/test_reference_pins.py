@@ -117,6 +117,23 @@ def test_oracle_hermite_matches_reference(pins):
     assert np.abs(dW.numpy() - g["herm_dW"]).max() < 1e-10
 
 
+@pytest.mark.parametrize("nt,D", R.XCHG_CASES)
+def test_exchange_split_matches_reference(pins, nt, D):
+    """The callbacks of one exchange: the same column widths in the same order as the reference's _exchange, so
+    that every LAMMPS comm buffer stays below 2^31 elements (meta tensors: sizes only, no memory)."""
+    from mace_onegpu.mliap_threepass import _exchange, exchange_blocks
+
+    calls = []
+    _exchange(lambda s, d, w: calls.append((s.shape[1], w)), torch.empty(nt, D, device="meta"),
+              torch.empty(nt, D, device="meta"), D)
+    assert np.array_equal(np.array(calls, dtype=np.int64), pins["g"][f"xchg_{nt}_{D}"])
+    blocks = exchange_blocks(nt, D)
+    assert [w for _, w in blocks] == [w for _, w in calls]
+    assert blocks[0][0] == 0 and all(b[0] + b[1] == c[0] for b, c in zip(blocks, blocks[1:]))
+    assert blocks[-1][0] + blocks[-1][1] == D
+    assert all(nt * w < 2 ** 31 - 1 or w == 1 for _, w in blocks)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", ["mliap", "ghost", "alloy"])
 def test_cuda_matches_reference_mliap(pins, case):
