@@ -19,9 +19,13 @@ What it restates (reference citations are paths inside ShiQiaoL/mace-million):
   evaluation with x clamped to [0, M - 1 - 1e-4] as in ``mace_onegpu/spline_w.py:18-27``, the derivative taken at
   the clamped point as the reference's backward kernel does, ``spline_w.py:53-75``).
 
-Parity with mace-torch / e3nn itself is unpinned (neither library is installed); the invariants the reference's own
-tests check (three-pass == full graph, chunk invariance, periodic replica, fp32 vs fp64) plus rotation / inversion
-invariance and finite differences pin this restatement (tests/test_oracle.py).
+Pinning: the reference's own driver code (ThreePassMLIAP.compute_forces with FastLayers, ReceiverChunkMACE,
+conv_spline.build_tables, spline_radial._hermite_eval, _exchange) was run on the CPU with this module's blocks behind
+mace-torch's module interface (tests/golden/make_reference_pins.py); this restatement reproduces its outputs to
+fp64 round-off (tests/test_reference_pins.py), which pins the three-pass driver, the layer order, the ML-IAP
+semantics and the tables against the reference itself.  The block math (mace-torch / e3nn, not installed) stays
+unpinned; the invariants the reference's own tests check (three-pass == full graph, chunk invariance, periodic
+replica, fp32 vs fp64) plus rotation / inversion invariance and finite differences pin it (tests/test_oracle.py).
 """
 from __future__ import annotations
 
