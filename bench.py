@@ -14,7 +14,9 @@ be installed: mace-torch / e3nn / cuEquivariance are absent) on a bounded sample
 Multi-GPU (torchrun, one rank per GPU): spatial domain decomposition of the periodic box (2x1x1, 2x2x1, 2x2x2 blocks)
 with explicit ghost atoms (shell r_max + 2 A skin) and the H1 forward / G1 reverse halo exchanges as NCCL grouped
 send/recv inside every timed step.  --scaling weak (default) keeps 1.03M atoms per GPU (the global box grows with N,
-BASELINE config 5 at N = 8); --scaling strong splits the 1.03M-atom box over the N GPUs.
+BASELINE config 5 at N = 8); --scaling strong splits the 1.03M-atom box over the N GPUs.  The decomposition is
+built on the GPU (domain.DeviceDecomposition).  `md` times --md-steps velocity-Verlet steps of the same box at every
+N (one GPU: md.VelocityVerlet; N GPUs: md.DomainVelocityVerlet on the same domains).
 """
 from __future__ import annotations
 
@@ -76,7 +78,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-replica-check", action="store_true", help="multi-GPU: skip the single-GPU comparison")
-    ap.add_argument("--md-steps", type=int, default=10, help="single GPU: MD steps timed after the bench (0: none)")
+    ap.add_argument("--md-steps", type=int, default=10, help="MD steps timed after the bench (0: none)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="multi-GPU: run the halo exchanges between whole passes instead of overlapping them with "
                          "interior chunks")
@@ -211,31 +213,49 @@ def run_reference(args, cfg, rank):
 
 
 # ------------------------------------------------------------------------------------------------ MD
-def md_timing(args, cfg, m, eng, dev):
-    """Velocity-Verlet MD on the configuration's box (BASELINE config 3's schedule: dt 1 fs, Verlet skin 2 A,
-    Maxwell-Boltzmann velocities at 300 K; mace_onegpu/md.py), timed over args.md_steps steps with CUDA events after
-    the force-evaluation timing.  The random-init model (energy scale 100) heats water within tens of fs, so this
-    is a timing figure of the MD loop (force evaluation, Verlet-list filter / rebuild, integration), not physics."""
+def md_timing(args, cfg, m, eng, dev, world=1, rank=0, grid=(1, 1, 1)):
+    """Velocity-Verlet MD on the bench's box (BASELINE config 3's schedule: dt 1 fs, Verlet skin 2 A,
+    Maxwell-Boltzmann velocities at 300 K), timed over args.md_steps steps with CUDA events after the
+    force-evaluation timing (max over ranks).  One GPU: mace_onegpu.md.VelocityVerlet.  N GPUs: DomainVelocityVerlet
+    on the same domains as the force bench (replicated positions, each rank's domain forces with the halo
+    exchanges, one force all-reduce per step, decomposition and Verlet lists rebuilt on the GPU).  The random-init
+    model (energy scale 100) heats water within tens of fs, so this is a timing figure of the MD loop (force
+    evaluation, Verlet-list filter / rebuild, integration), not physics."""
     import torch
 
     from mace_onegpu import structures as S
-    from mace_onegpu.md import VelocityVerlet
+    from mace_onegpu.md import DomainVelocityVerlet, VelocityVerlet
 
-    pos, Z, box = build_structure(cfg)
+    pos, Z, box = build_structure(cfg, grid if args.scaling == "weak" else (1, 1, 1))
     cols = S.species_columns(Z, m.arch.atomic_numbers)
     vel = S.maxwell_boltzmann(Z, 300.0, seed=0)
-    md = VelocityVerlet(eng, pos, box, cols, Z, vel, dt=1.0, skin=2.0)
+    if world == 1:
+        md = VelocityVerlet(eng, pos, box, cols, Z, vel, dt=1.0, skin=args.skin)
+    else:
+        import torch.distributed as dist
+
+        md = DomainVelocityVerlet(eng, pos, box, cols, Z, vel, grid, rank, dt=1.0, skin=args.skin,
+                                  overlap=not args.no_overlap)
     md.step()                                           # warm-up step
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     t0.record()
     for _ in range(args.md_steps):
         md.step()
     t1.record()
     torch.cuda.synchronize()
-    sps = args.md_steps / (t0.elapsed_time(t1) * 1e-3)
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    sps = args.md_steps / (ms * 1e-3)
     out = {"md_ns_per_day": sps * 1.0 * 86400 / 1e6, "steps_per_s": sps, "steps": args.md_steps, "dt_fs": 1.0,
-           "skin_A": 2.0, "neighbour_rebuilds": md.rebuilds,
+           "skin_A": args.skin, "atoms": len(Z), "neighbour_rebuilds": md.rebuilds,
+           "driver": "VelocityVerlet" if world == 1 else "DomainVelocityVerlet (replicated positions, domain forces, "
+                                                         "one force all-reduce per step)",
            "note": "random-init model: a timing figure of the MD loop, not a physical trajectory"}
     del md
     torch.cuda.empty_cache()
@@ -339,11 +359,12 @@ def main():
         pos, Z, box = build_structure(cfg, grid if args.scaling == "weak" else (1, 1, 1))
         n_cell = len(Z) // (world if args.scaling == "weak" else 1)
         cols_all = torch.as_tensor(S.species_columns(Z, m.arch.atomic_numbers))
-        dec = DM.Decomposition(pos, box, grid, m.arch.r_max + args.skin)
+        dec = DM.DeviceDecomposition(torch.as_tensor(pos, device=dev), box, grid, m.arch.r_max + args.skin)
         p, gid, n = dec.rank_atoms(rank)
-        nt = len(gid)
+        nt = int(gid.numel())
         pi, pj, rij = NB.neighbor_list_open(p, n, m.arch.r_max, device=dev)
-        cols = cols_all[torch.as_tensor(gid)]
+        cols = cols_all[gid.cpu()]
+        del dec, p
         hx = DM.HaloExchange(dec, rank, dev)
         parallelism = (f"domain {grid[0]}x{grid[1]}x{grid[2]}, NCCL halo exchange "
                        f"({'between passes' if args.no_overlap else 'overlapped with interior chunks'}), "
@@ -446,8 +467,8 @@ def main():
         mli._eng.pass_timing = False
 
     md = None
-    if world == 1 and args.md_steps > 0:
-        md = md_timing(args, cfg, m, eng, dev)
+    if args.md_steps > 0:
+        md = md_timing(args, cfg, m, eng, dev, world, rank, grid if world > 1 else (1, 1, 1))
 
     replica = None
     if world > 1 and not args.no_replica_check:

@@ -137,6 +137,111 @@ class Decomposition:
         return self.local_index[gh[sel, 0]]
 
 
+class DeviceDecomposition:
+    """The same decomposition as ``Decomposition`` (same owners, local order, ghost sets and ghost order), computed
+    with torch on the positions' device, so that a GPU builds it for millions of atoms in well under a second (the
+    numpy construction takes about a minute per 2M atoms): the multi-GPU bench and the MD driver, which rebuilds it
+    whenever the Verlet lists are rebuilt.  Index arrays are int64 tensors on that device; ``local`` and ``ghost`` are
+    per-rank lists of them.
+
+    Every (rank, atom, image) ghost entry is packed into one int64 key, (rank * N + atom) * 27 + image code, so the
+    deduplication and the (owner rank, owner-local index, image) ghost order are single sorts."""
+
+    def __init__(self, pos, box, grid, r_ghost: float):
+        pos = torch.as_tensor(pos, dtype=torch.float64)
+        dev = pos.device
+        box = torch.as_tensor(np.asarray(box, dtype=np.float64), device=dev)
+        pos = torch.remainder(pos, box)
+        g = torch.as_tensor(np.asarray(grid, dtype=np.int64), device=dev)
+        self.box, self.r_ghost, self.device = box, float(r_ghost), dev
+        self.grid = np.asarray(grid, dtype=np.int64)
+        self.nranks = int(self.grid.prod())
+        n = pos.shape[0]
+        w = box / g
+        if bool((w < 1e-9).any()):
+            raise ValueError("empty domain")
+        gm1 = g - 1
+        rg = self.r_ghost
+
+        def linear(c):
+            return (c[:, 0] * g[1] + c[:, 1]) * g[2] + c[:, 2]
+
+        cell = torch.minimum(torch.floor(pos / w).long(), gm1)
+        self.owner = linear(cell)
+        keys = []
+        for s in itertools.product((-1, 0, 1), repeat=3):
+            st = torch.tensor(s, dtype=torch.float64, device=dev)
+            q = pos + st * box
+            near = ((q > -rg) & (q < box + rg)).all(1)
+            ids = torch.nonzero(near).squeeze(1)
+            if ids.numel() == 0:
+                continue
+            qq = q[ids]
+            dlo = torch.clamp(torch.floor((qq - rg) / w).long(), min=0).minimum(gm1)
+            dhi = torch.clamp(torch.floor((qq + rg) / w).long(), min=0).minimum(gm1)
+            span = int((dhi - dlo).max()) + 1
+            code = (s[0] + 1) * 9 + (s[1] + 1) * 3 + s[2] + 1
+            for off in itertools.product(range(span), repeat=3):
+                d = dlo + torch.tensor(off, dtype=torch.int64, device=dev)
+                okd = (d <= dhi).all(1)
+                dd, ii, qd = d[okd], ids[okd], qq[okd]
+                lo = dd.double() * w
+                hi = lo + w
+                keep = ((qd >= lo - rg) & (qd < hi + rg)).all(1)
+                if not any(s):
+                    keep &= ~((qd >= lo) & (qd < hi)).all(1)
+                if bool(keep.any()):
+                    keys.append((linear(dd[keep]) * n + ii[keep]) * 27 + code)
+        E = torch.unique(torch.cat(keys)) if keys else torch.zeros(0, dtype=torch.int64, device=dev)
+        e_rank, e_atom, e_code = E // (27 * n), (E // 27) % n, E % 27
+        boundary = torch.zeros(n, dtype=torch.bool, device=dev)
+        boundary[e_atom] = True
+        # local atoms: interior first, then boundary atoms, each group in global order (as Decomposition)
+        order = torch.sort(self.owner * 2 + boundary.long(), stable=True).indices
+        counts = torch.bincount(self.owner, minlength=self.nranks).tolist()
+        self.local = list(torch.split(order, counts))
+        self.n_interior = [int((~boundary[idx]).sum()) for idx in self.local]
+        local_index = torch.empty(n, dtype=torch.int64, device=dev)
+        for idx in self.local:
+            local_index[idx] = torch.arange(idx.numel(), device=dev)
+        self.local_index = local_index
+        self.ghost = []
+        for r in range(self.nranks):
+            sel = e_rank == r
+            a, c = e_atom[sel], e_code[sel]
+            k = torch.sort((self.owner[a] * n + local_index[a]) * 27 + c).indices
+            self.ghost.append(torch.stack([a[k], c[k]], 1))          # [n_ghost, (global atom, image code)]
+        self.pos = pos
+
+    def image_shift(self, code):
+        code = torch.as_tensor(code, device=self.device)
+        s = torch.stack([code // 9 - 1, (code // 3) % 3 - 1, code % 3 - 1], -1)
+        return s.double() * self.box
+
+    def rank_atoms(self, r, pos=None):
+        """(positions [nl + ng, 3] with ghosts at their image positions, global atom ids, nl); `pos` replaces the
+        positions the decomposition was built from (same atoms, e.g. later MD positions)."""
+        pos = self.pos if pos is None else pos
+        loc, gh = self.local[r], self.ghost[r]
+        p = torch.cat([pos[loc], pos[gh[:, 0]] + self.image_shift(gh[:, 1])], 0)
+        return p, torch.cat([loc, gh[:, 0]]), int(loc.numel())
+
+    def recv_blocks(self, r):
+        """{owner rank: (start, stop)} ghost-row ranges of rank r (row index counted from nl)."""
+        own = self.owner[self.ghost[r][:, 0]]
+        uniq, cnt = torch.unique_consecutive(own, return_counts=True)
+        out, start = {}, 0
+        for o, c in zip(uniq.tolist(), cnt.tolist()):
+            out[int(o)] = (start, start + int(c))
+            start += int(c)
+        return out
+
+    def send_list(self, r, p):
+        """Owner-local indices (on rank r) of the ghost block rank p receives from r, in p's ghost order."""
+        gh = self.ghost[p]
+        return self.local_index[gh[self.owner[gh[:, 0]] == r, 0]]
+
+
 class HaloExchange:
     """The H1 forward / G1 reverse exchanges of one rank for feature rows [nt, D] (torch.distributed P2P)."""
 

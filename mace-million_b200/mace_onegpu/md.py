@@ -85,6 +85,76 @@ class VelocityVerlet:
         self.v += 0.5 * self.dt * ACC * self.F / self.m
 
 
+class DomainVelocityVerlet(VelocityVerlet):
+    """Velocity Verlet on N GPUs over spatial domains (one process per GPU, torch.distributed).
+
+    Every rank keeps all positions, velocities and forces of the system: they are replicated and stay bitwise
+    identical on all ranks. Each rank evaluates only the forces of its own domain's atoms: local receivers, local
+    or ghost senders, with the H1 / G1 halo exchanges of domain.HaloExchange. One all-reduce of the [N, 3] force
+    array (and of the energy) per step then gives every rank every force, and each rank integrates all atoms.
+
+    The decomposition (owners, ghost images within r_max + skin, exchange maps) and the Verlet lists (r_max + skin)
+    are rebuilt together, on the device (domain.DeviceDecomposition), when any atom has moved more than skin / 2
+    since the last build. Between rebuilds ownership and the ghost sets stay fixed, as between LAMMPS
+    reneighborings: a pair within r_max now was within r_max + skin of a receiver inside its domain at the build.
+    The rebuild decision needs no communication, because all ranks see the same positions.
+
+    engine: anything with the ThreePassEngine calls used here (device, model.r_max, plan, evaluate).
+    overlap: run the exchanges overlapped with interior chunks (evaluate(plan, halo=...)), else between the passes.
+    """
+
+    def __init__(self, engine, pos, box, elems, Z, vel, grid, rank: int, dt: float = 1.0, skin: float = 2.0,
+                 overlap: bool = True, group=None):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        self.grid, self.rank, self.overlap = tuple(int(g) for g in grid), int(rank), bool(overlap)
+        super().__init__(engine, pos, box, elems, Z, vel, dt=dt, skin=skin)
+
+    def _build(self):
+        from . import domain as DM
+
+        self.x = torch.remainder(self.x, self.box)
+        dec = DM.DeviceDecomposition(self.x, self.box, self.grid, self.r_max + self.skin)
+        p, gid, nl = dec.rank_atoms(self.rank)
+        self.dec, self.gid, self.nl = dec, gid, nl
+        self.cols = self.elems[gid]
+        self.hx = DM.HaloExchange(dec, self.rank, self.x.device, group=self.group)
+        _, self.vpj, _, self.vrow = NB.neighbor_list_open(p, nl, self.r_max + self.skin, device=self.x.device,
+                                                          return_rowptr=True)
+        self.x_ref = self.x.clone()
+        self.rebuilds += 1
+
+    def _pairs(self):
+        """Pairs within r_max at the current positions: local atoms and the fixed ghost images, no wrap."""
+        p, _, _ = self.dec.rank_atoms(self.rank, pos=self.x)
+        if p.is_cuda:
+            return NB.verlet_filter(p, self.box, self.vrow, self.vpj, self.r_max, periodic=False)
+        rows = torch.repeat_interleave(torch.arange(self.nl, device=p.device), self.vrow[1:] - self.vrow[:-1])
+        vpj = self.vpj.long()
+        d = p[rows] - p[vpj]
+        keep = (d * d).sum(1) < self.r_max * self.r_max
+        return rows[keep].to(torch.int32), self.vpj[keep], d[keep]
+
+    def _forces(self):
+        pi, pj, rij = self._pairs()
+        nt = int(self.gid.numel())
+        plan = self.eng.plan(pi, pj, rij, self.cols, self.nl, nt)
+        if self.overlap:
+            eat, pf = self.eng.evaluate(plan, halo=self.hx)
+        else:
+            eat, pf = self.eng.evaluate(plan, self.hx.forward, self.hx.reverse)
+        Fl = torch.zeros(nt, 3, dtype=torch.float64, device=self.x.device)
+        Fl.index_add_(0, pi.long(), -pf)
+        Fl.index_add_(0, pj.long(), pf)
+        F = torch.zeros_like(self.x)
+        F.index_add_(0, self.gid, Fl)                   # ghost images add onto the atoms they copy
+        e = eat.double().sum().reshape(1)
+        self.dist.all_reduce(F, group=self.group)
+        self.dist.all_reduce(e, group=self.group)
+        return F, float(e.item())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", default="water_1m", choices=["water_1m", "water_24k", "water_192"])

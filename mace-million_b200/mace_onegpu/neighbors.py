@@ -61,17 +61,19 @@ def _cuda_pairs(pos, n_recv: int, lo, width, nc, box, periodic: bool, r_cut: flo
     return (pi, pj, rij, rowptr) if return_rowptr else (pi, pj, rij)
 
 
-def verlet_filter(pos, box, vrow, vj, r_cut: float):
-    """Pairs of the skin list (CSR vrow int64 [n + 1], vj int32) within r_cut at positions `pos` (CUDA, periodic
-    minimum image in `box`): (pi int32, pj int32, rij fp64 [P, 3]) in the skin list's order."""
+def verlet_filter(pos, box, vrow, vj, r_cut: float, periodic: bool = True):
+    """Pairs of the skin list (CSR vrow int64 [n + 1], vj int32) within r_cut at positions `pos` (CUDA; minimum
+    image in `box` when periodic, plain differences for an open set with explicit ghost images): (pi int32,
+    pj int32, rij fp64 [P, 3]) in the skin list's order."""
     from . import _native as N
 
     L = N.lib()
     st = torch.cuda.current_stream(pos.device).cuda_stream
     n = vrow.numel() - 1
     box_a = _d3(torch.as_tensor(box).tolist())
+    per = 1 if periodic else 0
     counts = torch.empty(n, dtype=torch.int32, device=pos.device)
-    N.check(L.mace_b200_verlet_filter(N.ptr(pos), ctypes.addressof(box_a), 1, n, N.ptr(vrow), N.ptr(vj),
+    N.check(L.mace_b200_verlet_filter(N.ptr(pos), ctypes.addressof(box_a), per, n, N.ptr(vrow), N.ptr(vj),
                                       float(r_cut), N.ptr(counts), None, None, None, None, None, st), "verlet_filter")
     rowptr = torch.zeros(n + 1, dtype=torch.int64, device=pos.device)
     rowptr[1:] = torch.cumsum(counts, 0)
@@ -80,7 +82,7 @@ def verlet_filter(pos, box, vrow, vj, r_cut: float):
     pj = torch.empty(P, dtype=torch.int32, device=pos.device)
     rij = torch.empty(P, 3, dtype=torch.float64, device=pos.device)
     status = torch.zeros(1, dtype=torch.int32, device=pos.device)
-    N.check(L.mace_b200_verlet_filter(N.ptr(pos), ctypes.addressof(box_a), 1, n, N.ptr(vrow), N.ptr(vj),
+    N.check(L.mace_b200_verlet_filter(N.ptr(pos), ctypes.addressof(box_a), per, n, N.ptr(vrow), N.ptr(vj),
                                       float(r_cut), None, N.ptr(rowptr), N.ptr(pi), N.ptr(pj), N.ptr(rij),
                                       N.ptr(status), st), "verlet_filter")
     if int(status.item()):
@@ -137,16 +139,16 @@ def neighbor_list(pos, box, r_max: float, device="cpu", return_rowptr: bool = Fa
     return tuple(t.to(device) for t in _host_pairs(pos, N, r_max, box, return_rowptr))
 
 
-def neighbor_list_open(pos, n_recv: int, r_max: float, device="cpu"):
+def neighbor_list_open(pos, n_recv: int, r_max: float, device="cpu", return_rowptr: bool = False):
     """Pairs of an open (non-periodic) point set with explicit ghost images: receivers are atoms [0, n_recv),
     senders any atom, 0 < |x_i - x_j| < r_max.  CUDA device: the cell-list kernels over the bounding box (cells
     >= r_max, 27 neighbours without wrap); host: a k-d tree.  Returns (pi int32, pj int32, rij fp64 = x_i - x_j)
-    sorted by (pi, pj)."""
+    sorted by (pi, pj), and the receiver row pointer int64 [n_recv + 1] with return_rowptr."""
     pos = torch.as_tensor(pos, dtype=torch.float64, device=device).contiguous()
     if pos.is_cuda:
         lo = pos.min(0).values
         ext = pos.max(0).values - lo
         nc = torch.clamp((ext / r_max).floor().long(), min=1)
         width = torch.maximum(ext / nc, torch.full_like(ext, r_max))
-        return _cuda_pairs(pos, n_recv, lo, width, nc, lo, False, r_max)
-    return _host_pairs(pos, n_recv, r_max)
+        return _cuda_pairs(pos, n_recv, lo, width, nc, lo, False, r_max, return_rowptr)
+    return _host_pairs(pos, n_recv, r_max, return_rowptr=return_rowptr)

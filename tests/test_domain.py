@@ -39,6 +39,26 @@ def test_ghosts_reproduce_minimum_image_pairs(grid):
     assert got == ref
 
 
+@pytest.mark.parametrize("grid,r_ghost", [((2, 1, 1), 8.0), ((1, 2, 1), 8.0), ((2, 2, 1), 8.0), ((2, 2, 2), 8.0),
+                                          ((3, 1, 1), 8.0), ((4, 2, 1), 7.5), ((1, 1, 1), 8.0)])
+def test_device_decomposition_equals_numpy(grid, r_ghost):
+    """DeviceDecomposition (torch, used on the GPU by the multi-GPU bench and MD) builds exactly the numpy
+    construction: owners, local order, ghost sets and ghost order, exchange maps, rank positions."""
+    pos, Z, box = S.water_box(10, 9, 8, seed=5)
+    a = D.Decomposition(pos, box, grid, r_ghost)
+    b = D.DeviceDecomposition(torch.as_tensor(pos), box, grid, r_ghost)
+    assert np.array_equal(a.owner, b.owner.numpy())
+    for r in range(a.nranks):
+        assert np.array_equal(a.local[r], b.local[r].numpy())
+        assert np.array_equal(a.ghost[r], b.ghost[r].numpy())
+        assert a.n_interior[r] == b.n_interior[r] and a.recv_blocks(r) == b.recv_blocks(r)
+        for p in range(a.nranks):
+            assert np.array_equal(a.send_list(r, p), b.send_list(r, p).numpy())
+        pa, ga, na = a.rank_atoms(r)
+        pb, gb, nb = b.rank_atoms(r)
+        assert na == nb and np.array_equal(ga, gb.numpy()) and np.array_equal(pa, pb.numpy())
+
+
 @pytest.mark.parametrize("grid", [(2, 1, 1), (1, 2, 1)])
 def test_interior_atoms_first_have_no_ghost_neighbours(grid):
     """Each rank's local atoms are ordered interior first: receivers [0, n_interior) have only local senders and are

@@ -111,3 +111,90 @@ def test_two_gpu_domain_decomposition_matches_oracle(overlap):
     e0, F0 = _oracle()
     assert np.abs(E - e0.numpy()).max() < 1e-5
     assert np.abs(F - F0).max() < 1e-3
+
+
+MD_STEPS = 8
+MD_REBUILD_AT = 4      # one forced rebuild (wraps positions, new domains and lists) besides the automatic ones
+
+
+def _md_worker(rank, world, port, out_q):
+    """DomainVelocityVerlet over 2 GPUs; rank 0 then runs the single-GPU VelocityVerlet on the same box."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from mace_onegpu.engine import ThreePassEngine
+    from mace_onegpu.md import DomainVelocityVerlet, VelocityVerlet
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        mdl = M.default_model(0)
+        pos, Z, box = S.water_box(16, 8, 8, seed=2)
+        cols = S.species_columns(Z, mdl.arch.atomic_numbers)
+        vel = S.maxwell_boltzmann(Z, 300.0, seed=0)
+        eng = ThreePassEngine(mdl, sorted(set(cols.tolist())), chunk=256, device=dev)
+        md = DomainVelocityVerlet(eng, pos, box, cols, Z, vel, (2, 1, 1), rank, dt=1.0, skin=1.0)
+        E = [md.epot]
+        for k in range(MD_STEPS):
+            if k == MD_REBUILD_AT:
+                md._build()
+            md.step()
+            E.append(md.epot)
+        torch.cuda.synchronize()
+        x2, v2 = md.x.cpu().numpy(), md.v.cpu().numpy()
+        xs = [torch.zeros_like(md.x) for _ in range(world)]
+        dist.all_gather(xs, md.x)
+        same = all(torch.equal(xs[0], t) for t in xs)
+        nb2 = md.rebuilds
+        del md
+        dist.barrier()
+        if rank == 0:
+            one = VelocityVerlet(eng, pos, box, cols, Z, vel, dt=1.0, skin=1.0)
+            E1 = [one.epot]
+            for k in range(MD_STEPS):
+                if k == MD_REBUILD_AT:
+                    one._build()
+                one.step()
+                E1.append(one.epot)
+            out_q.put((x2, v2, np.array(E), nb2, same, one.x.cpu().numpy(), one.v.cpu().numpy(), np.array(E1),
+                       one.rebuilds, len(Z), np.asarray(box)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_md_matches_single_gpu_md():
+    """Eight velocity-Verlet steps (dt 1 fs, skin 1 A; the decomposition and Verlet lists are rebuilt on the GPU at
+    least once along the way) over 2 GPUs follow the single-GPU trajectory to within the fp32 force noise, and the
+    replicated positions stay identical on both ranks.  Positions are compared under minimum image: a rebuild wraps
+    them into the box."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_md_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p_ in procs:
+        p_.start()
+    t0 = time.time()
+    while True:
+        try:
+            res = q.get(timeout=2)
+            break
+        except queue.Empty:
+            dead = [p_.exitcode for p_ in procs if p_.exitcode not in (None, 0)]
+            assert not dead and time.time() - t0 < 600, f"rank failed: exit codes {dead}"
+    for p_ in procs:
+        p_.join(timeout=120)
+        assert p_.exitcode == 0
+    x2, v2, E2, nb2, same, x1, v1, E1, nb1, n, box = res
+    assert same
+    assert nb2 == nb1 >= 2
+    d = x2 - x1
+    d -= box * np.round(d / box)
+    assert np.abs(d).max() < 1e-5
+    assert np.abs(v2 - v1).max() < 1e-5
+    assert np.abs(E2 - E1).max() < 1e-5 * n
