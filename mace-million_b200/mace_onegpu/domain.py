@@ -150,7 +150,7 @@ class DeviceDecomposition:
     def __init__(self, pos, box, grid, r_ghost: float):
         pos = torch.as_tensor(pos, dtype=torch.float64)
         dev = pos.device
-        box = torch.as_tensor(np.asarray(box, dtype=np.float64), device=dev)
+        box = torch.as_tensor(box, dtype=torch.float64).to(dev)      # numpy, list or tensor on any device
         pos = torch.remainder(pos, box)
         g = torch.as_tensor(np.asarray(grid, dtype=np.int64), device=dev)
         self.box, self.r_ghost, self.device = box, float(r_ghost), dev
