@@ -364,8 +364,8 @@ def main():
         nt = int(gid.numel())
         pi, pj, rij = NB.neighbor_list_open(p, n, m.arch.r_max, device=dev)
         cols = cols_all[gid.cpu()]
-        del dec, p
         hx = DM.HaloExchange(dec, rank, dev)
+        del dec, p
         parallelism = (f"domain {grid[0]}x{grid[1]}x{grid[2]}, NCCL halo exchange "
                        f"({'between passes' if args.no_overlap else 'overlapped with interior chunks'}), "
                        f"ghost shell {m.arch.r_max + args.skin:g} A, {hx.n_interior} interior atoms on rank 0")
