@@ -162,9 +162,9 @@ def test_tc_planes_are_the_swizzled_split():
 
 
 def test_dedup_tables_merges_only_identical():
-    a = torch.randn(3, 5, 4)
+    a = torch.randn(3, 5, 4, generator=torch.Generator().manual_seed(0))
     cub = torch.stack([a[0], a[1], a[0], a[2], a[1].clone()])
-    cub[4, 2, 1] += 1e-7                       # one ulp-scale difference keeps its own table
+    cub[4, 2, 1] = torch.nextafter(cub[4, 2, 1], torch.tensor(float("inf")))   # one ulp apart: its own table
     t, m = E.dedup_tables(cub)
     assert m.tolist() == [0, 1, 0, 2, 3]
     assert t.shape[0] == 4
