@@ -92,7 +92,7 @@ def _worker(rank, world, port, grid, out_q):
 
     from oracle import mace_ref
 
-    torch.set_num_threads(2)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         mdl = M.default_model(0)
