@@ -15,7 +15,8 @@ oracle's restatement of mace-torch / e3nn.
 collide with this repository's ``mace_onegpu``) with three stand-ins for what this container lacks, active only
 inside the ``with`` block: ``ase.data.chemical_symbols`` (read by ThreePassMLIAP.__init__), ``e3nn.o3.Irreps(s).dim``
 (read by FastLayers.__init__ for the skip widths) and a no-op ``torch.cuda.synchronize`` (the reference synchronises
-between passes; there is no CUDA device here).
+between passes; there is no CUDA device here).  Bytecode writing is off inside the block, so that importing leaves
+the reference checkout untouched.
 
 Layouts inside the adapter: flat features are mace's "mul_ir" order, per irrep a [channel][component] block
 (index c * (2l + 1) + m); h1 rows are the oracle's [C, 4] (0e | 1o) flattened, which only the adapter's own blocks
@@ -84,9 +85,10 @@ def reference_env(ref_root):
     for name, mod in {**_fake_e3nn(), **_fake_ase()}.items():
         if name not in sys.modules:
             stand_ins[name] = mod
-    sync = torch.cuda.synchronize
+    sync, nobytecode = torch.cuda.synchronize, sys.dont_write_bytecode
     sys.modules.update(stand_ins)
     torch.cuda.synchronize = lambda *a, **k: None
+    sys.dont_write_bytecode = True              # the reference checkout is read-only: no __pycache__ there
     try:
         _load_package(ref_root)
 
@@ -95,7 +97,7 @@ def reference_env(ref_root):
 
         yield mod
     finally:
-        torch.cuda.synchronize = sync
+        torch.cuda.synchronize, sys.dont_write_bytecode = sync, nobytecode
         for name in stand_ins:
             sys.modules.pop(name, None)
 
