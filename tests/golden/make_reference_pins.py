@@ -19,6 +19,9 @@ Cases (reference code that ran, inputs, what is stored):
 * ``rc``: ReceiverChunkMACE.compute (receiver_chunk_mace.py:260-388) on the reference's System (Morton order, its
   own cell-list neighbour list) with LocalGraph padding (pad=True), FastLayers installed as the reference's
   fast_layers.install does, chunk 64: total energy and atom forces (original atom order).
+* ``rc_ace``: the same ReceiverChunkMACE run with the reference's exact density-projection layer 1
+  (ace_layer1.py:23-105, installed over FastLayers as ace_layer1.install does).  Its path table (fused_edge_conv.
+  path_table reads it from cuEquivariance, absent here) is this build's layer-1 channelwise TP table, the same terms.
 * ``tables``: conv_spline.build_tables (conv_spline.py:230-249) for species (H, O), 512 knots over [0.5, r_max]:
   knot rows 0, 1, 255, 510, 511 of TV and TG (fp32) of every ordered species pair, both interaction blocks.
 * ``xchg``: mliap_threepass._exchange (mliap_threepass.py:40-55) on meta tensors (no memory) of ntotal x D arrays
@@ -145,6 +148,25 @@ def main(ref_root):
         Fo = torch.empty_like(F)
         Fo[sysm.perm] = F
         out.update(rc_energy=np.float64(E), rc_F=Fo.numpy(), rc_n_pairs=np.int64(int(sysm.NN.sum())))
+
+        fec, ace = mod("fused_edge_conv"), mod("ace_layer1")
+        t1 = M.tp_tables()[0]
+        table = dict(C=int(mdl.arch.channels), nW=t1["nW"], nX=t1["nX"], nY=t1["nY"], nO=t1["nO"],
+                     terms=[(int(w), int(k), int(m), int(o), float(c)) for (w, k, m, o, c) in t1["terms"]])
+        saved_table = fec.path_table
+        fec.path_table = lambda block: table
+        try:
+            cs = sorted(torch.unique(cols).tolist())
+            fl.install(adapter, cs)
+            ace.install(adapter, cs)
+            E, F, _t, _p = rc.ReceiverChunkMACE(adapter, torch.float64, 64, pad=True, node_bucket=256).compute(
+                sysm, log=lambda *a: None)
+        finally:
+            rc.layer1, rc.layer2_energy = saved
+            fec.path_table = saved_table
+        Fo = torch.empty_like(F)
+        Fo[sysm.perm] = F
+        out.update(rc_ace_energy=np.float64(E), rc_ace_F=Fo.numpy())
 
         zs = [1, 8]
         tab = mod("conv_spline").build_tables(adapter, zs, n_grid=512, r_lo=0.5, device="cpu")

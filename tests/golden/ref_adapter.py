@@ -18,9 +18,12 @@ inside the ``with`` block: ``ase.data.chemical_symbols`` (read by ThreePassMLIAP
 between passes; there is no CUDA device here).  Bytecode writing is off inside the block, so that importing leaves
 the reference checkout untouched.
 
-Layouts inside the adapter: flat features are mace's "mul_ir" order, per irrep a [channel][component] block
-(index c * (2l + 1) + m); h1 rows are the oracle's [C, 4] (0e | 1o) flattened, which only the adapter's own blocks
-read (the reference stores H1 rows without looking inside).
+Layouts inside the adapter: the tensor product's output (the "mid" features between conv_tp and linear) is
+cuEquivariance's "ir_mul" order, per irrep a [component][channel] block (index o * C + c), which the reference's
+ACELayer1 writes itself (its 'seg' layout); the other flat features are "mul_ir", per irrep a [channel][component]
+block (index c * (2l + 1) + m); h1 rows are the oracle's [C, 4] (0e | 1o) flattened, which only the adapter's own
+blocks read (the reference stores H1 rows without looking inside).  The radial MLP is a sequence of layer modules
+with the attributes of e3nn's FullyConnectedNet layers that ACELayer1 reads (h_in, weight, act, var_in, var_out).
 """
 from __future__ import annotations
 
@@ -119,6 +122,22 @@ def _unflat(x, ls, C):
     return out
 
 
+def _flat_ir(parts):
+    """list of [n, C, 2l+1] -> [n, sum (2l+1) C] in ir_mul order (index o * C + c)."""
+    return torch.cat([p.transpose(1, 2).reshape(p.shape[0], -1) for p in parts], -1)
+
+
+def _unflat_ir(x, ls, C):
+    """inverse of _flat_ir for the irreps ls."""
+    out, o = [], 0
+    for l in ls:
+        w = C * (2 * l + 1)
+        out.append(x[:, o:o + w].reshape(x.shape[0], 2 * l + 1, C).transpose(1, 2))
+        o += w
+    assert o == x.shape[1], (o, x.shape)
+    return out
+
+
 def _species(node_attrs):
     """Column of each one-hot row (the reference builds node_attrs with one_hot; the blocks here need one-hot)."""
     s = node_attrs.argmax(1)
@@ -150,6 +169,20 @@ class _Fn(torch.nn.Module):
         return self.fn(*args)
 
 
+class _FCLayer(torch.nn.Module):
+    """One layer of the bias-free radial MLP, y = act * silu(h W / sqrt(h_in)) (act = the normalize2mom constant) or,
+    for the last layer (act None), y = h W / sqrt(h_in): the oracle's radial_mlp step by step."""
+
+    def __init__(self, W, act):
+        super().__init__()
+        self.register_buffer("weight", W)
+        self.h_in, self.act, self.var_in, self.var_out = int(W.shape[0]), act, 1, 1
+
+    def forward(self, h):
+        z = h @ self.weight / math.sqrt(self.h_in)
+        return z if self.act is None else self.act * torch.nn.functional.silu(z)
+
+
 class _Interaction(torch.nn.Module):
     def __init__(self, ref: mace_ref.MaceRef, i: int):
         super().__init__()
@@ -172,11 +205,15 @@ class _Interaction(torch.nn.Module):
 
             self.linear_up = _Fn(up)
         self.nirr = nirr
-        self.conv_tp_weights = _Fn(lambda feats: ref.radial_mlp(i, feats))
+        nl = 0
+        while f"interactions.{i}.conv_tp_weights.{nl + 1}" in P:
+            nl += 1
+        self.conv_tp_weights = torch.nn.Sequential(
+            *[_FCLayer(P[f"interactions.{i}.conv_tp_weights.{k}"], ref.cst if k < nl else None) for k in range(nl + 1)])
         w = P[f"interactions.{i}.density_fn.weight"]
         self.density_fn = _Fn(lambda feats: feats @ w.unsqueeze(-1) / math.sqrt(w.shape[0]))
         self.conv_tp = _Fn(self._conv)
-        self.linear = _Fn(lambda msg: _flat(ref.linear_mid(i, _unflat(msg, self.mid_ls, C))))
+        self.linear = _Fn(lambda msg: _flat(ref.linear_mid(i, _unflat_ir(msg, self.mid_ls, C))))
         self.skip_tp = _Fn(self._skip)
         self.reshape = _Fn(lambda x: torch.cat(_unflat(x, [0, 1, 2, 3], C), -1))
 
@@ -189,7 +226,7 @@ class _Interaction(torch.nn.Module):
             v = node_feats.reshape(n, C, 4)
             X = [v[:, :, 0:1], v[:, :, 1:4]]
         mid = self.ref.conv(self.i, X, edge_attrs, tp_weights, edge_index[0].long(), edge_index[1].long(), n)
-        return _flat(mid)
+        return _flat_ir(mid)
 
     def _skip(self, x, node_attrs):
         """FullyConnectedTensorProduct(x, one-hot species): per-species channel mixing, 1/sqrt(C Z)."""

@@ -9,8 +9,8 @@ and shift 0.25; the ML-IAP entry point also ran on a 250-atom 16-element alloy (
 FastLayers' SpeciesSkip).
 
 CPU: the oracle's own three-pass reproduces those outputs: per-atom energies to 1e-12 eV, pair forces to 1e-6 eV/A
-(the reference accumulates pair forces in fp32; measured 5.3e-8), the receiver-chunk run's total energy to 1e-9 eV
-and atom forces to 1e-10 eV/A, the tables bit for bit (fp32) and the Hermite lookup and its derivative to 1e-10.
+(the reference accumulates pair forces in fp32; measured 5.3e-8), the receiver-chunk runs' total energy to 1e-9 eV
+and atom forces to 1e-10 eV/A (with FastLayers, and with the reference's exact density-projection layer 1), the tables bit for bit (fp32) and the Hermite lookup and its derivative to 1e-10.
 GPU: the CUDA path (512-knot tables) through ThreePassMLIAP.compute_forces reproduces the reference's ML-IAP outputs
 (exact radial MLP) within the north_star tolerances, 1e-5 eV per atom and 1e-3 eV/A per pair force, without and with
 ghost atoms and a shuffled pair list, and on the 16-element alloy (direct layer-1 form, per-species GEMM problems)."""
@@ -78,15 +78,18 @@ def test_oracle_matches_reference_mliap(pins, oracle_runs, case):
     assert np.abs(pf.numpy() - g[f"{case}_pf"]).max() < 1e-6
 
 
-def test_oracle_matches_reference_receiver_chunk(pins, oracle_runs):
+@pytest.mark.parametrize("run", ["rc", "rc_ace"])
+def test_oracle_matches_reference_receiver_chunk(pins, oracle_runs, run):
+    """ReceiverChunkMACE with FastLayers ("rc") and with the reference's exact density-projection layer 1 installed
+    over it ("rc_ace", ace_layer1.py): the same energy and atom forces as the oracle's standard three-pass."""
     from oracle import mace_ref
 
     g = pins["g"]
     pi, pj, _, _, n = pins["mliap"]
     eat, pf = oracle_runs["mliap"]
     F = mace_ref.atom_forces(pi, pj, pf, n).numpy()
-    assert abs(float(eat.sum()) - float(g["rc_energy"])) < 1e-9
-    assert np.abs(F - g["rc_F"]).max() < 1e-10
+    assert abs(float(eat.sum()) - float(g[f"{run}_energy"])) < 1e-9
+    assert np.abs(F - g[f"{run}_F"]).max() < 1e-10
 
 
 def test_oracle_tables_match_reference_build_tables(pins):
