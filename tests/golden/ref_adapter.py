@@ -3,8 +3,9 @@
 The reference's driver code (ShiQiaoL/mace-million, ``mace_onegpu/``) needs only torch: the ML-IAP entry point
 ``mliap_threepass.py:155-616`` (ThreePassMLIAP.compute_forces), the three-pass evaluator
 ``receiver_chunk_mace.py:82-388`` (Morton-ordered System, LocalGraph chunk topology with padding, ReceiverChunkMACE),
-the receiver-only layer order ``fast_layers.py:20-223`` (FastLayers, SpeciesSkip) and the spline tables
-``conv_spline.py:230-249`` / ``spline_radial.py:37-151``.  What it calls into is mace-torch / e3nn / cuEquivariance
+the receiver-only layer order ``fast_layers.py:20-223`` (FastLayers, SpeciesSkip), the exact density-projection
+layer 1 ``ace_layer1.py:23-105`` (ACELayer1), the exchange column split ``mliap_threepass.py:40-55`` and the spline
+tables ``conv_spline.py:230-249`` / ``spline_radial.py:37-151``.  What it calls into is mace-torch / e3nn / cuEquivariance
 (absent here): the model's blocks.  ``OracleMACE`` gives the reference that model interface (the attribute names and
 call signatures of mace-torch 0.3.15's ScaleShiftMACE with RealAgnosticDensity(Residual)InteractionBlock), each block
 evaluated by ``oracle.mace_ref.MaceRef`` in fp64.  Running the reference's code on it pins the oracle's three-pass
@@ -187,7 +188,6 @@ class _Interaction(torch.nn.Module):
     def __init__(self, ref: mace_ref.MaceRef, i: int):
         super().__init__()
         self.ref, self.i, C = ref, i, ref.C
-        nirr = [0] if i == 0 else [0, 1]
         self.mid_ls = [lo for (lo, _a, _b) in ref.inst[i]]
         P = ref.P
         if i == 0:
@@ -204,7 +204,6 @@ class _Interaction(torch.nn.Module):
                     / math.sqrt(C)
 
             self.linear_up = _Fn(up)
-        self.nirr = nirr
         nl = 0
         while f"interactions.{i}.conv_tp_weights.{nl + 1}" in P:
             nl += 1
