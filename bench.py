@@ -162,9 +162,14 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------ CPU baseline
+CPU_CHUNK = 64      # the oracle's receiver chunk on the host: fastest there (chunk 16,384: 10x slower, page-fault bound)
+
+
 def cpu_baseline(cfg, n_side: int):
     """The oracle (fp64 torch restatement of the three-pass evaluation, 512-knot tables) on a water box of
-    n_side^3 molecules, all host threads.  Returns (atoms/s, seconds, cores, atoms)."""
+    n_side^3 molecules, all host threads, receiver chunks of CPU_CHUNK (the chunk changes only the size of the
+    intermediates, not the arithmetic; 32-64 run fastest on the host, e.g. 78 against 7.5 atoms/s at 16,384 on a
+    375-atom box with 8 cores).  Returns (atoms/s, seconds, cores, atoms)."""
     import dataclasses
 
     import torch
@@ -185,7 +190,7 @@ def cpu_baseline(cfg, n_side: int):
     pi, pj, rij = NB.neighbor_list(pos, box, m.arch.r_max)
     ref = mace_ref.MaceRef(m.params(), dataclasses.asdict(m.arch), spline_knots=512)
     t0 = time.perf_counter()
-    ref.three_pass(pi, pj, rij, cols, len(Z), 16384)
+    ref.three_pass(pi, pj, rij, cols, len(Z), CPU_CHUNK)
     dt = time.perf_counter() - t0
     return len(Z) / dt, dt, cores, len(Z)
 
@@ -200,7 +205,7 @@ def run_reference(args, cfg, rank):
             vals.append((v, dt))
     value = statistics.median(v for v, _ in vals)
     ms = statistics.median(dt for _, dt in vals) * 1e3
-    sample = (f"oracle fp64 three-pass (512-knot tables) on a {cfg['kind']} box of {n} atoms "
+    sample = (f"oracle fp64 three-pass (512-knot tables, chunk {CPU_CHUNK}) on a {cfg['kind']} box of {n} atoms "
               f"({args.cpu_sample}^3 molecules) per step; atoms/s of this O(N) evaluation, which the per-atom cost "
               f"extrapolates linearly to the {cfg['desc'].split(':')[0]}")
     line = {"metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -478,7 +483,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, cores, na = cpu_baseline(cfg, args.cpu_sample)
         cpu = {"value": v, "unit": "atoms/s", "cores": cores, "kind": "port",
-               "sample": f"oracle fp64 three-pass (512-knot tables) on a {na}-atom {cfg['kind']} box "
+               "sample": f"oracle fp64 three-pass (512-knot tables, chunk {CPU_CHUNK}) on a {na}-atom {cfg['kind']} box "
                          f"({args.cpu_sample}^3 molecules), {dt:.1f} s; atoms/s of this O(N) evaluation, "
                          f"extrapolated linearly per atom to the workload"}
 
