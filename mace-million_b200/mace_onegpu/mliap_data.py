@@ -11,7 +11,6 @@ Ghost atoms are described by an owner map (owner[j] = local atom of which ghost 
 """
 from __future__ import annotations
 
-import numpy as np
 import torch
 
 

@@ -19,8 +19,9 @@ What it restates (reference citations are paths inside ShiQiaoL/mace-million):
   evaluation with x clamped to [0, M - 1 - 1e-4] as in ``mace_onegpu/spline_w.py:18-27``, the derivative taken at
   the clamped point as the reference's backward kernel does, ``spline_w.py:53-75``).
 
-Pinning: the reference's own driver code (ThreePassMLIAP.compute_forces with FastLayers, ReceiverChunkMACE,
-conv_spline.build_tables, spline_radial._hermite_eval, _exchange) was run on the CPU with this module's blocks behind
+Pinning: the reference's own driver code (ThreePassMLIAP.compute_forces with FastLayers, ReceiverChunkMACE with
+FastLayers and with ace_layer1's density-projection layer 1, conv_spline.build_tables, spline_radial._hermite_eval,
+_exchange) was run on the CPU with this module's blocks behind
 mace-torch's module interface (tests/golden/make_reference_pins.py); this restatement reproduces its outputs to
 fp64 round-off (tests/test_reference_pins.py), which pins the three-pass driver, the layer order, the ML-IAP
 semantics and the tables against the reference itself.  The block math (mace-torch / e3nn, not installed) stays
@@ -31,7 +32,6 @@ from __future__ import annotations
 
 import math
 
-import numpy as np
 import torch
 
 from . import o3_ref

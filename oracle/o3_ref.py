@@ -13,7 +13,6 @@ basis is the standard real combination of complex SH, whose convention cancels i
 from __future__ import annotations
 
 import functools
-import itertools
 import math
 
 import numpy as np
