@@ -1,5 +1,5 @@
-"""Multi-GPU MD driver logic on the CPU (gloo, world size 2): md.DomainVelocityVerlet against the single-process
-md.VelocityVerlet on the same periodic box.
+"""Multi-GPU MD driver logic on the CPU (gloo, world sizes 2, 4 and 8 on the bench's grids): md.DomainVelocityVerlet
+against the single-process md.VelocityVerlet on the same periodic box.
 
 The force provider is a stand-in with the ThreePassEngine calls the drivers use (plan / evaluate, with or without a
 halo): a smooth pair potential phi(r) = eps (1 - r / rc)^4 on the given pair list, per-atom energy 1/2 sum phi over
@@ -67,12 +67,13 @@ def _single():
     return md.x.numpy(), md.v.numpy(), np.array(E), md.rebuilds
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, grid, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import torch.distributed as dist
 
     from mace_onegpu.md import DomainVelocityVerlet
 
+    torch.set_num_threads(1)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         pos, Z, box, vel, cols = _system()
@@ -83,7 +84,7 @@ def _worker(rank, world, port, q):
                 super()._build()
                 eng.gid = self.gid
 
-        md = Tracked(eng, pos, box, cols, Z, vel, (2, 1, 1), rank, dt=2.0, skin=SKIN)
+        md = Tracked(eng, pos, box, cols, Z, vel, grid, rank, dt=2.0, skin=SKIN)
         E = [md.epot]
         for _ in range(STEPS):
             md.step()
@@ -93,17 +94,25 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_domain_md_matches_single_process():
+@pytest.fixture(scope="module")
+def single():
+    return _single()
+
+
+@pytest.mark.parametrize("grid", [(2, 1, 1), (2, 2, 1), (2, 2, 2)], ids=["2-ranks", "4-ranks", "8-ranks"])
+def test_domain_md_matches_single_process(single, grid):
+    """The 2, 4 and 8-rank grids of the multi-GPU bench (2x1x1, 2x2x1, 2x2x2)."""
     import torch.multiprocessing as mp
 
-    x1, v1, E1, nb1 = _single()
+    x1, v1, E1, nb1 = single
+    world = int(np.prod(grid))
     assert nb1 >= 3                                          # the run crosses several rebuilds
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, grid, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=300) for _ in procs]
@@ -117,7 +126,7 @@ def test_domain_md_matches_single_process():
         assert nb == nb1
         assert np.abs(x - x1).max() < 1e-9 and np.abs(v - v1).max() < 1e-9
         assert np.abs(E - E1).max() < 1e-9 * max(1.0, np.abs(E1).max())
-    assert np.array_equal(out[0][1], out[1][1])              # replicated positions identical on both ranks
+    assert all(np.array_equal(out[0][1], o[1]) for o in out)  # replicated positions identical on every rank
 
 
 if __name__ == "__main__":
