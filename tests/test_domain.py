@@ -153,3 +153,21 @@ def test_two_rank_gloo_three_pass_matches_single_process(grid):
     F0 = mace_ref.atom_forces(pi, pj, pf0, len(Z)).numpy()
     assert np.abs(E - e0.numpy()).max() < 1e-9
     assert np.abs(F - F0).max() < 1e-9
+
+
+def test_device_decomposition_atoms_on_domain_faces():
+    """Atoms exactly on domain faces, at the box origin and one ulp below the box length: both constructions put
+    them in the same domains and ghost sets."""
+    pos, Z, box = S.water_box(10, 9, 8, seed=6)
+    w = box / np.array([2, 2, 2])
+    pos = pos.copy()
+    pos[0] = [w[0], w[1], w[2]]                          # on three faces at once
+    pos[1] = [0.0, 0.0, 0.0]
+    pos[2] = np.nextafter(box, 0.0)                       # just inside the upper box faces
+    pos[3] = [w[0] - 8.0, w[1] + 8.0, 0.5 * w[2]]          # exactly one ghost shell from a face
+    a = D.Decomposition(pos, box, (2, 2, 2), 8.0)
+    b = D.DeviceDecomposition(torch.as_tensor(pos), box, (2, 2, 2), 8.0)
+    assert np.array_equal(a.owner, b.owner.numpy())
+    for r in range(a.nranks):
+        assert np.array_equal(a.local[r], b.local[r].numpy())
+        assert np.array_equal(a.ghost[r], b.ghost[r].numpy())

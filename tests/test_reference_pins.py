@@ -137,6 +137,25 @@ def test_exchange_split_matches_reference(pins, nt, D):
     assert all(nt * w < 2 ** 31 - 1 or w == 1 for _, w in blocks)
 
 
+def test_exchange_blocks_properties():
+    """For any size: the blocks tile the columns in order, all but the last have the same width D >> k, k is the
+    smallest shift for which a block stays below 2^31 - 1 elements (or the width is one column)."""
+    from mace_onegpu.mliap_threepass import exchange_blocks
+
+    rng = np.random.default_rng(5)
+    for _ in range(2000):
+        nt = int(rng.integers(1, 2 ** 33))
+        D = int(rng.integers(1, 2049))
+        blocks = exchange_blocks(nt, D)
+        w = blocks[0][1]
+        assert [c0 for c0, _ in blocks] == list(range(0, D, w))
+        assert all(bw == w for _, bw in blocks[:-1]) and 0 < blocks[-1][1] <= w
+        assert sum(bw for _, bw in blocks) == D
+        assert nt * w < 2 ** 31 - 1 or w == 1
+        k = next(k for k in range(64) if (D >> k) == w)
+        assert k == 0 or (nt * (D >> (k - 1)) >= 2 ** 31 - 1 and (D >> (k - 1)) > 1)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", ["mliap", "ghost", "alloy"])
 def test_cuda_matches_reference_mliap(pins, case):
