@@ -18,7 +18,8 @@ Cases (reference code that ran, inputs, what is stored):
   seeded E0): FastLayers' SpeciesSkip over 16 species columns, per-species E0, chunk 96.
 * ``rc``: ReceiverChunkMACE.compute (receiver_chunk_mace.py:260-388) on the reference's System (Morton order, its
   own cell-list neighbour list) with LocalGraph padding (pad=True), FastLayers installed as the reference's
-  fast_layers.install does, chunk 64: total energy and atom forces (original atom order).
+  fast_layers.install does, chunk 64: total energy and atom forces (original atom order), and a checksum of its
+  neighbour list's (receiver, sender) pairs in the original atom order.
 * ``rc_ace``: the same ReceiverChunkMACE run with the reference's exact density-projection layer 1
   (ace_layer1.py:23-105, installed over FastLayers as ace_layer1.install does).  Its path table (fused_edge_conv.
   path_table reads it from cuEquivariance, absent here) is this build's layer-1 channelwise TP table, the same terms.
@@ -138,6 +139,13 @@ def main(ref_root):
         sysm = rc.System(torch.as_tensor(pos, dtype=torch.float64), torch.as_tensor(box), cols.clone(),
                          float(mdl.arch.r_max), "cpu")
         sysm.build_neighbors()
+        # its neighbour list (System.build_neighbors, receiver_chunk_mace.py:113-165) as (receiver, sender) pairs in
+        # the original atom order, sorted like this build's host list
+        rows = torch.repeat_interleave(torch.arange(sysm.N), sysm.NN.long())
+        senders = sysm.NL.long()[sysm.NL >= 0]
+        gi, gj = sysm.perm[rows], sysm.perm[senders]
+        o = torch.argsort(gi * sysm.N + gj)
+        out["rc_pair_checksum"] = np.int64(pair_checksum(gi[o], gj[o]))
         saved = rc.layer1, rc.layer2_energy
         try:
             fl.install(adapter, sorted(torch.unique(cols).tolist()))

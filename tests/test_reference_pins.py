@@ -63,6 +63,8 @@ def test_fixture_inputs_reproduced(pins):
     gpi, gpj, _, gcols = pins["ghost"][:4]
     assert pi.numel() == int(g["n_pairs"]) == int(g["rc_n_pairs"])
     assert R.pair_checksum(pi, pj) == int(g["pair_checksum"])
+    # this build's host neighbour list has exactly the pairs of the reference's System.build_neighbors
+    assert R.pair_checksum(pi, pj) == int(g["rc_pair_checksum"])
     assert R.pair_checksum(gpi, gpj) == int(g["ghost_checksum"]) and gcols.numel() == int(g["n_total_ghost"])
     api, apj, _, acols, _ = pins["alloy"]
     assert R.pair_checksum(api, apj) == int(g["alloy_checksum"])
