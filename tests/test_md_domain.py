@@ -115,7 +115,16 @@ def test_domain_md_matches_single_process(single, grid):
     procs = [ctx.Process(target=_worker, args=(r, world, port, grid, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=300) for _ in procs]
+    import queue
+    import time
+
+    out, t0 = [], time.time()
+    while len(out) < world:
+        try:
+            out.append(q.get(timeout=2))
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead and time.time() - t0 < 300, f"rank failed: exit codes {dead}"
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
